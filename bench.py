@@ -1,0 +1,363 @@
+#!/usr/bin/env python3
+"""Benchmark of the f32 matmul hot path (Momiru's frozen-plan GEMM node) on B200.
+
+Workload (default): M = N = K = 8192 f32 with the fused epilogue
+C = ReLU(A @ B + bias); A, B uniform[-1,1) (SplitMix64 seeds 1, 2), bias
+normal(0, 0.1) (seed 3), StrictFp32 math (3xTF32 on tcgen05). One step is one
+bound replay of that node. On N GPUs the output columns are dealt out in
+256-column tile units, each rank computes its column block and the blocks are
+all-gathered so every rank holds the whole C (total work fixed: strong
+scaling).
+
+  value   TFLOP/s of the whole job, device-timed (inputs resident in HBM)
+  e2e     the same metric through the public API with host buffers: per step
+          H2D of A, B, bias from pinned memory, the replay, D2H of C
+  roofline the dominant kernel's achieved TFLOP/s against the TF32-derived
+          peak (measured bf16 dense peak / 2, divided by 3 for 3xTF32)
+
+`--impl reference` times the reference's CPU GEMM (restated, oracle/) on the
+host cores on a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FLUSH_NOTE = "inputs (A,B: 512 MiB) larger than the 126 MB L2; no flush needed"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--mode", choices=["strict", "tf32"], default="strict")
+    ap.add_argument("--size", type=int, default=8192)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p.get("hbm_gbs", 6650.0), "bf16_tflops": p.get("bf16_tflops", 1590.0),
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", 1400.0), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi sampled every 100 ms while `active` is set."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.samples = []
+        self.active = False
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if self.active:
+                self.samples.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for i, n in enumerate(names):
+                if len(s) > 5 + i and s[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        pw = [float(s[3]) for s in self.samples if s[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.samples),
+                "power_w_max": max(pw) if pw else None}
+
+
+def cpu_baseline_sample(a, b, bias, seconds: float):
+    """The reference's CPU GEMM (gemm_avx2 loop structure, restated in oracle/)
+    on all host threads over a bounded row sample of the same workload."""
+    from oracle import oracle as O
+    O.build()
+    n = a.shape[1]
+    nthreads = os.cpu_count() or 1
+    rows = nthreads
+    t0 = time.perf_counter()
+    O.gemm_avx2_restated(a[:rows], b, 0, rows, nthreads)
+    dt = time.perf_counter() - t0
+    per_row_batch = max(dt, 1e-3)
+    reps = max(1, int(seconds / per_row_batch))
+    rows_total = min(a.shape[0], rows * reps)
+    t0 = time.perf_counter()
+    O.gemm_avx2_restated(a[:rows_total], b, 0, rows_total, nthreads)
+    dt = time.perf_counter() - t0
+    flops = 2.0 * rows_total * n * a.shape[1]
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
+            "sample": f"{rows_total} of {a.shape[0]} output rows of the {a.shape[0]}x{n}x{a.shape[1]} GEMM "
+                      f"(restated gemm_avx2, -O3 -mavx2 -ffp-contract=off, row-sharded), {dt:.1f} s"}
+
+
+def dist_init(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def run_reference(args, rank, world):
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    from momiru_b200 import rng
+    from oracle import oracle as O
+    O.build()
+    n = args.size
+    nthreads = os.cpu_count() or 1
+    a = rng.randu((n, n), 1)
+    b = rng.randu((n, n), 2)
+    # size the per-step row sample so the whole run takes a few minutes at most
+    t0 = time.perf_counter()
+    O.gemm_avx2_restated(a[:nthreads], b, 0, nthreads, nthreads)
+    dt = max(time.perf_counter() - t0, 1e-3)
+    total_steps = args.steps + args.warmup
+    budget = 120.0 / max(total_steps, 1)
+    rows = min(n, max(nthreads, int(nthreads * budget / dt)))
+    for _ in range(args.warmup):
+        O.gemm_avx2_restated(a[:rows], b, 0, rows, nthreads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.gemm_avx2_restated(a[:rows], b, 0, rows, nthreads)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    flops = 2.0 * rows * n * n
+    value = flops / t / 1e12
+    line = {
+        "impl": "reference", "metric": "f32 GEMM TFLOP/s @8192^3 (C=ReLU(A@B+bias))", "value": value,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (SplitMix64 uniform[-1,1))",
+        "config": {"workload": f"gemm_{n}x{n}x{n}_bias_relu", "m": n, "n": n, "k": n},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
+                         "sample": f"{rows} of {n} output rows per step (restated gemm_avx2, "
+                                   f"row-sharded over {nthreads} threads)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_init(args)
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    from momiru_b200 import (AccuracyContract, BoundGemm, DeviceBuffer, DeviceView, Epilogue, KernelMathMode,
+                             MatMulNode, rng, shard_columns)
+
+    n = args.size
+    mode = KernelMathMode.StrictFp32 if args.mode == "strict" else KernelMathMode.Tf32
+    node = MatMulNode(math_mode=mode, epilogue=Epilogue.BIAS_RELU,
+                      accuracy=AccuracyContract.StrictFp32 if args.mode == "strict" else AccuracyContract.AllowTf32)
+    a_h = rng.randu((n, n), 1)
+    b_h = rng.randu((n, n), 2)
+    bias_h = rng.randn((n,), 3, 0.1)
+    dev = torch.device(f"cuda:{local}")
+    stream = torch.cuda.current_stream()
+    a_t = torch.from_numpy(a_h).to(dev)
+    b_t = torch.from_numpy(b_h).to(dev)
+    bias_t = torch.from_numpy(bias_h).to(dev)
+    c0, c1 = shard_columns(n, world, rank, 256)
+    ncols = c1 - c0
+    out_t = torch.empty((n, max(ncols, 4)), dtype=torch.float32, device=dev)
+    A = DeviceView.contiguous(DeviceBuffer.from_torch(a_t), (n, n))
+    B = DeviceView.contiguous(DeviceBuffer.from_torch(b_t), (n, n)).narrow(1, c0, ncols)
+    BIAS = DeviceView.contiguous(DeviceBuffer.from_torch(bias_t), (n,)).narrow(0, c0, ncols)
+    C = DeviceView.contiguous(DeviceBuffer.from_torch(out_t), (n, out_t.shape[1])).narrow(1, 0, ncols)
+    g = BoundGemm(node, A, B, C, BIAS, stream=stream.cuda_stream)
+    gathered = None
+    if world > 1:
+        gathered = torch.empty((world, n, out_t.shape[1]), dtype=torch.float32, device=dev)
+
+    def step():
+        g.replay()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out_t)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    g.quiesce_or_abort(60)
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.active = True
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        g.replay()
+        ev[i][1].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out_t)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    clocks.active = False
+    if world > 1:
+        dist.barrier()
+    g.quiesce_or_abort(60)
+    total_ms = t_start.elapsed_time(t_end)
+    kernel_ms = [s.elapsed_time(e) for s, e in ev]
+    ms_step = total_ms / args.steps
+    if world > 1:
+        tm = torch.tensor([ms_step], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ms_step = float(tm.item())
+    flops_total = 2.0 * n * n * n
+    value = flops_total / (ms_step * 1e-3) / 1e12
+
+    # ---------------------------------------------------------------- e2e
+    # Public API with host buffers: pinned H2D of this step's inputs, replay,
+    # D2H of the result, all inside the timed region.
+    a_pin = torch.from_numpy(a_h).pin_memory()
+    b_pin = torch.from_numpy(b_h).pin_memory()
+    bias_pin = torch.from_numpy(bias_h).pin_memory()
+    c_pin = torch.empty((n, out_t.shape[1]), dtype=torch.float32).pin_memory()
+    res_pin = torch.empty(gathered.shape, dtype=torch.float32).pin_memory() if world > 1 else c_pin
+    h2d = (a_pin.numel() + b_pin.numel() + bias_pin.numel()) * 4
+    d2h = res_pin.numel() * 4
+
+    def e2e_step():
+        a_t.copy_(a_pin, non_blocking=True)
+        b_t.copy_(b_pin, non_blocking=True)
+        bias_t.copy_(bias_pin, non_blocking=True)
+        g.replay()
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out_t)
+            res_pin.copy_(gathered, non_blocking=True)
+        else:
+            c_pin.copy_(out_t, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks.active = True
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks.active = False
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if world > 1:
+        tm = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tm.item())
+    g.quiesce_or_abort(60)
+    clocks.stop()
+
+    # ----------------------------------------------------------- roofline
+    peaks = load_peaks()
+    tf32_peak = peaks["bf16_tflops"] / 2.0
+    kern_ms = statistics.mean(kernel_ms)
+    shard_flops = 2.0 * n * ncols * n
+    achieved = shard_flops / (kern_ms * 1e-3) / 1e12
+    peak = tf32_peak / 3.0 if args.mode == "strict" else tf32_peak
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "tc_gemm_8192_strict_traffic.json")
+    if os.path.exists(prof) and args.size == 8192:
+        with open(prof) as f:
+            traffic = json.load(f).get(f"{args.mode}_bytes_per_launch_n{world}")
+
+    line = {
+        "metric": "f32 GEMM TFLOP/s @8192^3 (C=ReLU(A@B+bias)), % of TF32 peak", "value": value,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "math": "3xTF32 (StrictFp32)" if args.mode == "strict" else "TF32",
+        "data": "synthetic (SplitMix64 uniform[-1,1) A,B; normal(0,0.1) bias)",
+        "config": {"workload": f"gemm_{n}x{n}x{n}_bias_relu", "m": n, "n": n, "k": n,
+                   "parallelism": f"column-block x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "l2": FLUSH_NOTE},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "traffic": traffic,
+                     "peak_basis": (f"{peaks['source']} bf16 dense {peaks['bf16_tflops']} / 2 (TF32 rate)"
+                                    + (" / 3 (3xTF32)" if args.mode == "strict" else "")),
+                     "kernel_ms": kern_ms, "frac_of_tf32_peak": achieved / tf32_peak},
+        "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(a_h, b_h, bias_h, args.cpu_seconds)
+    g.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,182 @@
+/*
+ * momiru_gemm.h -- C ABI of the B200 (sm_100a) f32 matmul hot path.
+ *
+ * This is the drop-in boundary a GPU backend of Momiru's frozen-plan runtime
+ * binds. In the reference, a frozen GEMM node reaches a backend through two
+ * traits (src/momiru/tensor_light/execution/runtime.rs):
+ *
+ *   Backend::bind_resources            runtime.rs:954-988   -> mmr_gemm_bind
+ *   BoundBackend::execute_gpu_node     runtime.rs:886-890   -> mmr_gemm_run
+ *   BoundBackend::quiesce_or_abort     runtime.rs:944-946   -> mmr_gemm_quiesce
+ *   (drop of the bound backend)                            -> mmr_gemm_destroy
+ *
+ * and the node itself is Operation::MatMul{transpose_lhs, transpose_rhs}
+ * (src/momiru/tensor_light/execution/ir.rs:1468-1473) whose shape and
+ * broadcast contract is validation.rs:2300-2398. Device buffers follow
+ * BufferHandle::Device{device_ordinal, address, bytes} (runtime.rs:297-301);
+ * views follow Shape{dims, strides} plus a byte base offset
+ * (tensor/shape.rs:130-206, plan.rs:1285-1307).
+ *
+ * Conventions:
+ *   - Every entry point returns an int32 status (MMR_OK = 0). Nothing throws
+ *     or aborts across this boundary. mmr_last_error() gives a message for the
+ *     calling thread's last failure.
+ *   - Caller owns every buffer. A bound handle keeps raw device addresses; the
+ *     caller must keep the buffers alive until mmr_gemm_quiesce (or destroy)
+ *     has returned MMR_OK after the last run.
+ *   - Bind does all validation, kernel-family choice and TMA descriptor
+ *     encoding. Run only enqueues the pre-built launch on the bound stream:
+ *     no allocation, no planning, no descriptor encoding (runtime.rs:962-973).
+ */
+#ifndef MOMIRU_GEMM_H
+#define MOMIRU_GEMM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MMR_API __attribute__((visibility("default")))
+#else
+#define MMR_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (CpuNativeError / PlanError analogues, cpu.rs:290-306) */
+enum {
+  MMR_OK = 0,
+  MMR_ERR_INVALID_ARGUMENT = 1,   /* null pointer, bad enum value            */
+  MMR_ERR_INVALID_SHAPE = 2,      /* MatMul shape/broadcast contract broken  */
+  MMR_ERR_UNSUPPORTED_LAYOUT = 3, /* strides/offset/alignment not admissible */
+  MMR_ERR_UNSAFE_ALIASING = 4,    /* output overlaps an input                */
+  MMR_ERR_UNSUPPORTED_MATH = 5,   /* math mode vs accuracy contract mismatch */
+  MMR_ERR_UNSUPPORTED_DEVICE = 6, /* ordinal mismatch / not an sm_100 device  */
+  MMR_ERR_OUT_OF_BOUNDS = 7,      /* a view does not fit its bound buffer    */
+  MMR_ERR_CUDA = 8,               /* a CUDA runtime/driver call failed       */
+  MMR_ERR_NCCL = 9,               /* an NCCL call failed                     */
+  MMR_ERR_TIMEOUT = 10,           /* bounded wait expired (host or device)   */
+  MMR_ERR_DEVICE_FAULT_FLAG = 11, /* a kernel reported an error word         */
+  MMR_ERR_UNSUPPORTED_FAMILY = 12 /* forced kernel family cannot run this    */
+};
+
+/* ---- numeric mode (KernelMathMode, ir.rs:559-569; gated by the output's
+ *      AccuracyContract, validation.rs:3579-3640) */
+enum {
+  MMR_MATH_STRICT_FP32 = 0, /* 3xTF32 split on tcgen05; rel-Frobenius <= 1e-5 */
+  MMR_MATH_TF32 = 1,        /* one TF32 pass; needs AllowTf32; <= 2e-3        */
+  MMR_MATH_EXACT = 2        /* bit-exact with the reference CPU GEMM order   */
+};
+
+/* ---- fused epilogue: MatMul -> Add(bias[N] broadcast) -> Relu, expressed in
+ *      the reference as a FusedStaticDataflow node (plan.rs:1080-1106) */
+enum {
+  MMR_EPI_NONE = 0,
+  MMR_EPI_BIAS = 1,
+  MMR_EPI_BIAS_RELU = 2,
+  MMR_EPI_RELU = 3
+};
+
+/* ---- kernel family (KernelFamily, plan.rs:326-431); AUTO lets bind choose */
+enum {
+  MMR_FAMILY_AUTO = 0,
+  MMR_FAMILY_TCGEN05 = 1, /* TMA + tcgen05/TMEM tensor-core GEMM              */
+  MMR_FAMILY_GEMV = 2,    /* skinny-M (M <= 16) HBM-streaming kernel          */
+  MMR_FAMILY_SIMT = 3     /* CUDA-core kernel, any strides; bit-exact order  */
+};
+
+#define MMR_MAX_RANK 4
+
+/* A strided f32 view of a device buffer (Shape{dims,strides} + base offset).
+ * Strides are in elements and may be 0 only on broadcast (extent-1) axes. */
+typedef struct mmr_view {
+  uint64_t address;           /* device address of the bound buffer          */
+  uint64_t bytes;             /* bytes of the bound buffer from `address`     */
+  uint64_t base_offset_bytes; /* byte offset of element [0,..,0]              */
+  int32_t rank;               /* 1..MMR_MAX_RANK (0 = absent, for bias)       */
+  int32_t device_ordinal;
+  int64_t dims[MMR_MAX_RANK];
+  int64_t strides[MMR_MAX_RANK];
+  uint64_t allocation_id;     /* identity of the owning allocation; 0 = unknown */
+} mmr_view;
+
+/* The frozen GEMM node plus its storage bindings. */
+typedef struct mmr_matmul_desc {
+  mmr_view lhs, rhs, out;
+  mmr_view bias;              /* rank 1 [N] when the epilogue adds a bias     */
+  int32_t transpose_lhs;
+  int32_t transpose_rhs;
+  int32_t math_mode;          /* MMR_MATH_*                                   */
+  int32_t epilogue;           /* MMR_EPI_*                                    */
+  int32_t family;             /* MMR_FAMILY_*                                 */
+  int32_t device_ordinal;
+  void *stream;               /* cudaStream_t; NULL = legacy default stream  */
+} mmr_matmul_desc;
+
+/* What bind decided (for logging and tests). */
+typedef struct mmr_gemm_info {
+  int32_t family;             /* chosen MMR_FAMILY_*                          */
+  int32_t math_mode;
+  int64_t batch, m, n, k;
+  int32_t a_mn_major;         /* 1: A tile is M-contiguous (transposed view)  */
+  int32_t b_mn_major;         /* 1: B tile is N-contiguous (row-major B)      */
+  int32_t grid, block, cluster;
+  int32_t smem_bytes;
+  int32_t tile_m, tile_n, tile_k, stages;
+  int64_t tiles;
+  double flops;               /* 2*batch*M*N*K                                */
+  double bytes;               /* algorithmic HBM bytes (A + B + C [+ bias])   */
+} mmr_gemm_info;
+
+typedef struct mmr_gemm_handle mmr_gemm_handle;
+
+/* Host-only validation of the MatMul contract and layout admission; touches no
+ * GPU. Fills `info` (may be NULL). validation.rs:2300-2398, cpu.rs:613-714,
+ * runtime.rs:618-811. */
+MMR_API int32_t mmr_gemm_validate(const mmr_matmul_desc *desc, mmr_gemm_info *info);
+
+/* Bind: validate, choose the kernel family, encode TMA descriptors, create the
+ * completion event. Enqueues no work. runtime.rs:954-988. */
+MMR_API int32_t mmr_gemm_bind(const mmr_matmul_desc *desc, mmr_gemm_handle **out);
+
+/* Replay: enqueue the bound kernel on the bound stream. runtime.rs:886-890. */
+MMR_API int32_t mmr_gemm_run(mmr_gemm_handle *h);
+
+/* Replay on another stream (same device). */
+MMR_API int32_t mmr_gemm_run_on(mmr_gemm_handle *h, void *stream);
+
+/* Establish completion of every run on this handle, polling with a host
+ * deadline; also reads the device error word. runtime.rs:944-946. */
+MMR_API int32_t mmr_gemm_quiesce(mmr_gemm_handle *h, uint64_t timeout_ns);
+
+/* Release the handle (waits for completion first, bounded by 10 s). */
+MMR_API int32_t mmr_gemm_destroy(mmr_gemm_handle *h);
+
+MMR_API int32_t mmr_gemm_query(const mmr_gemm_handle *h, mmr_gemm_info *info);
+
+/* Message for the calling thread's last non-OK status. */
+MMR_API const char *mmr_last_error(void);
+
+/* Library version string and build flags. */
+MMR_API const char *mmr_version(void);
+
+/* ---- device-side bounded-wait self test (failure-detection path) ---------
+ * Launches one CTA that waits on an mbarrier nobody arrives at, with a limit
+ * of `limit_ns`; the kernel gives up, records MMR_ERR_TIMEOUT in its error
+ * word and returns, leaving the context usable. Returns the status the host
+ * read back (MMR_ERR_TIMEOUT is the expected, healthy answer). */
+MMR_API int32_t mmr_selftest_bounded_wait(int32_t device_ordinal, uint64_t limit_ns);
+
+/* ---- column-block sharding -------------------------------------------------
+ * Column range [col0, col1) of rank `rank` when N output columns are dealt to
+ * `nranks` ranks in whole units of `align` columns (the output-tile width).
+ * Pure host arithmetic. */
+MMR_API int32_t mmr_shard_columns(int64_t n, int32_t nranks, int32_t rank, int32_t align,
+                          int64_t *col0, int64_t *col1);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOMIRU_GEMM_H */

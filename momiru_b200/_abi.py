@@ -1,0 +1,134 @@
+"""ctypes bindings of the C ABI declared in include/momiru_gemm.h.
+
+The shared library is built in-tree (momiru_b200/lib/libmomiru_gemm.so) by
+momiru_b200/build.py. There is no fallback: if the library is missing the
+import of the execution layer fails loudly.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+MAX_RANK = 4
+
+# status codes
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_INVALID_SHAPE = 2
+ERR_UNSUPPORTED_LAYOUT = 3
+ERR_UNSAFE_ALIASING = 4
+ERR_UNSUPPORTED_MATH = 5
+ERR_UNSUPPORTED_DEVICE = 6
+ERR_OUT_OF_BOUNDS = 7
+ERR_CUDA = 8
+ERR_NCCL = 9
+ERR_TIMEOUT = 10
+ERR_DEVICE_FAULT_FLAG = 11
+ERR_UNSUPPORTED_FAMILY = 12
+
+MATH_STRICT_FP32, MATH_TF32, MATH_EXACT = 0, 1, 2
+EPI_NONE, EPI_BIAS, EPI_BIAS_RELU, EPI_RELU = 0, 1, 2, 3
+FAMILY_AUTO, FAMILY_TCGEN05, FAMILY_GEMV, FAMILY_SIMT = 0, 1, 2, 3
+FAMILY_NAMES = {FAMILY_AUTO: "auto", FAMILY_TCGEN05: "tcgen05", FAMILY_GEMV: "gemv", FAMILY_SIMT: "simt"}
+
+EXPORTED = [
+    "mmr_gemm_validate", "mmr_gemm_bind", "mmr_gemm_run", "mmr_gemm_run_on", "mmr_gemm_quiesce",
+    "mmr_gemm_destroy", "mmr_gemm_query", "mmr_last_error", "mmr_version",
+    "mmr_selftest_bounded_wait", "mmr_shard_columns",
+]
+
+
+class MmrView(ctypes.Structure):
+    _fields_ = [
+        ("address", ctypes.c_uint64),
+        ("bytes", ctypes.c_uint64),
+        ("base_offset_bytes", ctypes.c_uint64),
+        ("rank", ctypes.c_int32),
+        ("device_ordinal", ctypes.c_int32),
+        ("dims", ctypes.c_int64 * MAX_RANK),
+        ("strides", ctypes.c_int64 * MAX_RANK),
+        ("allocation_id", ctypes.c_uint64),
+    ]
+
+
+class MmrMatmulDesc(ctypes.Structure):
+    _fields_ = [
+        ("lhs", MmrView),
+        ("rhs", MmrView),
+        ("out", MmrView),
+        ("bias", MmrView),
+        ("transpose_lhs", ctypes.c_int32),
+        ("transpose_rhs", ctypes.c_int32),
+        ("math_mode", ctypes.c_int32),
+        ("epilogue", ctypes.c_int32),
+        ("family", ctypes.c_int32),
+        ("device_ordinal", ctypes.c_int32),
+        ("stream", ctypes.c_void_p),
+    ]
+
+
+class MmrGemmInfo(ctypes.Structure):
+    _fields_ = [
+        ("family", ctypes.c_int32),
+        ("math_mode", ctypes.c_int32),
+        ("batch", ctypes.c_int64),
+        ("m", ctypes.c_int64),
+        ("n", ctypes.c_int64),
+        ("k", ctypes.c_int64),
+        ("a_mn_major", ctypes.c_int32),
+        ("b_mn_major", ctypes.c_int32),
+        ("grid", ctypes.c_int32),
+        ("block", ctypes.c_int32),
+        ("cluster", ctypes.c_int32),
+        ("smem_bytes", ctypes.c_int32),
+        ("tile_m", ctypes.c_int32),
+        ("tile_n", ctypes.c_int32),
+        ("tile_k", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("tiles", ctypes.c_int64),
+        ("flops", ctypes.c_double),
+        ("bytes", ctypes.c_double),
+    ]
+
+    def as_dict(self) -> dict:
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libmomiru_gemm.so")
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the in-tree library (build it first with momiru_b200.build)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"momiru_b200: CUDA library not built ({LIB_PATH} missing); run `python -m momiru_b200.build`")
+    lib = ctypes.CDLL(LIB_PATH)
+    P = ctypes.POINTER
+    h = ctypes.c_void_p
+    lib.mmr_gemm_validate.argtypes = [P(MmrMatmulDesc), P(MmrGemmInfo)]
+    lib.mmr_gemm_bind.argtypes = [P(MmrMatmulDesc), P(h)]
+    lib.mmr_gemm_run.argtypes = [h]
+    lib.mmr_gemm_run_on.argtypes = [h, ctypes.c_void_p]
+    lib.mmr_gemm_quiesce.argtypes = [h, ctypes.c_uint64]
+    lib.mmr_gemm_destroy.argtypes = [h]
+    lib.mmr_gemm_query.argtypes = [h, P(MmrGemmInfo)]
+    lib.mmr_last_error.restype = ctypes.c_char_p
+    lib.mmr_version.restype = ctypes.c_char_p
+    lib.mmr_selftest_bounded_wait.argtypes = [ctypes.c_int32, ctypes.c_uint64]
+    lib.mmr_shard_columns.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                      P(ctypes.c_int64), P(ctypes.c_int64)]
+    for name in EXPORTED:
+        fn = getattr(lib, name)
+        if name not in ("mmr_last_error", "mmr_version"):
+            fn.restype = ctypes.c_int32
+    _lib = lib
+    return lib
+
+
+def last_error() -> str:
+    return load().mmr_last_error().decode(errors="replace")

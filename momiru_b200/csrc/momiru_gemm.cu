@@ -1,0 +1,880 @@
+// momiru_gemm.cu -- C ABI of the B200 f32 matmul hot path (include/momiru_gemm.h).
+//
+// Bind-time work (validation, kernel-family choice, TMA descriptor encoding,
+// event creation) happens once in mmr_gemm_bind; mmr_gemm_run only enqueues
+// the pre-built launch. This mirrors the reference runtime's split between
+// Backend::bind_resources and BoundBackend::execute_gpu_node
+// (src/momiru/tensor_light/execution/runtime.rs:879-988).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+
+#include "../../include/momiru_gemm.h"
+#include "gemv.cuh"
+#include "ptx.cuh"
+#include "simt_gemm.cuh"
+#include "tc_gemm.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int32_t fail(int32_t code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define MMR_CUDA_TRY(expr)                                                                      \
+  do {                                                                                          \
+    cudaError_t e_ = (expr);                                                                    \
+    if (e_ != cudaSuccess) return fail(MMR_ERR_CUDA, "%s: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+// Restores the caller's current device on scope exit.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess) ok = true;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+// ------------------------------------------------------------- the plan --
+
+// A logical matrix operand: element (batch b0, b1, row r, col c) lives at
+// base + b0*s_b0 + b1*s_b1 + r*s_r + c*s_c (elements; s_* >= 0).
+struct Operand {
+  uint64_t base = 0;  // device address of element [0,..,0]
+  int64_t s_b0 = 0, s_b1 = 0, s_r = 0, s_c = 0;
+  uint64_t lo = 0, hi = 0;  // byte range touched (for aliasing checks)
+  uint64_t alloc = 0;
+};
+
+struct Plan {
+  int64_t batch0 = 1, batch1 = 1, m = 0, n = 0, k = 0;
+  Operand a, b, c;
+  uint64_t bias = 0;
+  int64_t bias_s = 0;
+  int32_t epilogue = MMR_EPI_NONE;
+  int32_t math = MMR_MATH_STRICT_FP32;
+  int32_t family = MMR_FAMILY_AUTO;
+  int32_t device = 0;
+  bool empty = false;  // nothing to compute (some output extent is zero)
+};
+
+int64_t extent_elems(const mmr_view& v) {
+  // Largest element offset + 1 (0 when any extent is 0).
+  int64_t span = 0;
+  for (int i = 0; i < v.rank; ++i) {
+    if (v.dims[i] == 0) return 0;
+    span += (v.dims[i] - 1) * v.strides[i];
+  }
+  return span + 1;
+}
+
+int32_t check_view(const mmr_view& v, const char* name, int32_t device) {
+  if (v.rank < 1 || v.rank > MMR_MAX_RANK)
+    return fail(MMR_ERR_INVALID_SHAPE, "%s: rank %d outside 1..%d", name, v.rank, MMR_MAX_RANK);
+  for (int i = 0; i < v.rank; ++i) {
+    if (v.dims[i] < 0) return fail(MMR_ERR_INVALID_SHAPE, "%s: negative extent on axis %d", name, i);
+    if (v.strides[i] < 0)
+      return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: negative stride on axis %d is not admitted", name, i);
+    if (v.dims[i] > (int64_t(1) << 31) - 1)
+      return fail(MMR_ERR_INVALID_SHAPE, "%s: extent %lld on axis %d exceeds 2^31-1", name,
+                  (long long)v.dims[i], i);
+  }
+  if (v.base_offset_bytes % 4 != 0)
+    return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: base offset %llu is not f32-aligned", name,
+                (unsigned long long)v.base_offset_bytes);
+  if (v.address % 4 != 0) return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: address is not f32-aligned", name);
+  const int64_t ext = extent_elems(v);
+  if (ext > 0) {
+    if (v.address == 0) return fail(MMR_ERR_INVALID_ARGUMENT, "%s: null address", name);
+    const uint64_t need = v.base_offset_bytes + uint64_t(ext) * 4u;
+    if (need > v.bytes)
+      return fail(MMR_ERR_OUT_OF_BOUNDS, "%s: view needs %llu bytes but the buffer has %llu", name,
+                  (unsigned long long)need, (unsigned long long)v.bytes);
+  }
+  if (v.device_ordinal != device)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "%s: device ordinal %d differs from the node's %d", name,
+                v.device_ordinal, device);
+  return MMR_OK;
+}
+
+// canonical_broadcast_extent (src/momiru/tensor_light/execution/ir.rs:247-252):
+// equal -> that; 1 vs x -> x (so 0 vs 1 -> 0); otherwise incompatible.
+bool broadcast_extent(int64_t l, int64_t r, int64_t* out) {
+  if (l == r) { *out = l; return true; }
+  if (l == 1) { *out = r; return true; }
+  if (r == 1) { *out = l; return true; }
+  return false;
+}
+
+void set_range(Operand& o, const mmr_view& v) {
+  o.lo = v.address + v.base_offset_bytes;
+  o.hi = o.lo + uint64_t(extent_elems(v)) * 4u;
+  o.alloc = v.allocation_id;
+}
+
+bool ranges_overlap(const Operand& x, const Operand& y) {
+  if (x.lo == x.hi || y.lo == y.hi) return false;
+  return x.lo < y.hi && y.lo < x.hi;
+}
+
+// The MatMul node's shape and broadcast contract, following
+// validation.rs:2300-2398, plus the bind-time layout admission of
+// cpu.rs:613-714 / runtime.rs:618-811 restated for device views.
+int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
+  if (!d) return fail(MMR_ERR_INVALID_ARGUMENT, "null descriptor");
+  if (d->math_mode < MMR_MATH_STRICT_FP32 || d->math_mode > MMR_MATH_EXACT)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "unknown math mode %d", d->math_mode);
+  if (d->epilogue < MMR_EPI_NONE || d->epilogue > MMR_EPI_RELU)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "unknown epilogue %d", d->epilogue);
+  if (d->family < MMR_FAMILY_AUTO || d->family > MMR_FAMILY_SIMT)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "unknown kernel family %d", d->family);
+  p->epilogue = d->epilogue;
+  p->math = d->math_mode;
+  p->family = d->family;
+  p->device = d->device_ordinal;
+
+  const mmr_view &L = d->lhs, &R = d->rhs, &O = d->out;
+  int32_t rc;
+  if ((rc = check_view(L, "lhs", d->device_ordinal))) return rc;
+  if ((rc = check_view(R, "rhs", d->device_ordinal))) return rc;
+  if ((rc = check_view(O, "out", d->device_ordinal))) return rc;
+
+  const int lr = L.rank, rr = R.rank;
+  const bool ta = d->transpose_lhs != 0, tb = d->transpose_rhs != 0;
+  if ((lr == 1 && ta) || (rr == 1 && tb))
+    return fail(MMR_ERR_INVALID_SHAPE, "transpose flag on a rank-1 operand");
+  const bool lv = lr == 1, rv = rr == 1;
+
+  // Logical A [M,K] and B [K,N] with the promoted vector dims.
+  int64_t m, k1, k2, n;
+  Operand A, B, C;
+  A.base = L.address + L.base_offset_bytes;
+  B.base = R.address + R.base_offset_bytes;
+  C.base = O.address + O.base_offset_bytes;
+  if (lv) {
+    m = 1; k1 = L.dims[0]; A.s_r = 0; A.s_c = L.strides[0];
+  } else {
+    const int64_t rows = L.dims[lr - 2], cols = L.dims[lr - 1];
+    const int64_t sr = L.strides[lr - 2], sc = L.strides[lr - 1];
+    if (ta) { m = cols; k1 = rows; A.s_r = sc; A.s_c = sr; }
+    else    { m = rows; k1 = cols; A.s_r = sr; A.s_c = sc; }
+  }
+  if (rv) {
+    k2 = R.dims[0]; n = 1; B.s_r = R.strides[0]; B.s_c = 0;
+  } else {
+    const int64_t rows = R.dims[rr - 2], cols = R.dims[rr - 1];
+    const int64_t sr = R.strides[rr - 2], sc = R.strides[rr - 1];
+    if (tb) { k2 = cols; n = rows; B.s_r = sc; B.s_c = sr; }
+    else    { k2 = rows; n = cols; B.s_r = sr; B.s_c = sc; }
+  }
+  if (k1 != k2)
+    return fail(MMR_ERR_INVALID_SHAPE, "contraction mismatch: lhs K=%lld, rhs K=%lld", (long long)k1,
+                (long long)k2);
+  const int lbr = lv ? 0 : lr - 2, rbr = rv ? 0 : rr - 2;
+  const int br = std::max(lbr, rbr);
+  const int mat_rank = (lv ? 0 : 1) + (rv ? 0 : 1);
+  if (O.rank != br + mat_rank && !(br + mat_rank == 0 && O.rank == 1 && O.dims[0] == 1))
+    return fail(MMR_ERR_INVALID_SHAPE, "output rank %d, expected %d", O.rank, br + mat_rank);
+  if (br > 2) return fail(MMR_ERR_INVALID_SHAPE, "more than two batch axes");
+
+  int64_t bdims[2] = {1, 1};
+  int64_t as_b[2] = {0, 0}, bs_b[2] = {0, 0}, cs_b[2] = {0, 0};
+  for (int b = 0; b < br; ++b) {
+    const int li = b - (br - lbr), ri = b - (br - rbr);
+    const int64_t ld = li >= 0 ? L.dims[li] : 1, rd = ri >= 0 ? R.dims[ri] : 1;
+    int64_t e;
+    if (!broadcast_extent(ld, rd, &e))
+      return fail(MMR_ERR_INVALID_SHAPE, "batch axis %d: %lld vs %lld do not broadcast", b, (long long)ld,
+                  (long long)rd);
+    if (O.dims[b] != e)
+      return fail(MMR_ERR_INVALID_SHAPE, "output batch axis %d is %lld, expected %lld", b,
+                  (long long)O.dims[b], (long long)e);
+    // Place batch axes right-aligned into the two slots (slot 1 = innermost).
+    const int slot = 2 - br + b;
+    bdims[slot] = e;
+    as_b[slot] = (li >= 0 && ld != 1) ? L.strides[li] : 0;
+    bs_b[slot] = (ri >= 0 && rd != 1) ? R.strides[ri] : 0;
+    cs_b[slot] = O.strides[b];
+  }
+  int oax = br;
+  if (!lv) {
+    if (O.dims[oax] != m)
+      return fail(MMR_ERR_INVALID_SHAPE, "output rows %lld, expected %lld", (long long)O.dims[oax], (long long)m);
+    C.s_r = O.strides[oax];
+    ++oax;
+  }
+  if (!rv) {
+    if (O.dims[oax] != n)
+      return fail(MMR_ERR_INVALID_SHAPE, "output cols %lld, expected %lld", (long long)O.dims[oax], (long long)n);
+    C.s_c = O.strides[oax];
+  }
+  if (lv && !rv) C.s_r = 0;
+  if (rv && !lv) { C.s_r = O.strides[br]; C.s_c = 0; }
+  A.s_b0 = as_b[0]; A.s_b1 = as_b[1];
+  B.s_b0 = bs_b[0]; B.s_b1 = bs_b[1];
+  C.s_b0 = cs_b[0]; C.s_b1 = cs_b[1];
+  set_range(A, L);
+  set_range(B, R);
+  set_range(C, O);
+
+  // Aliasing: the output may not overlap an input (runtime.rs:540-551).
+  if (ranges_overlap(C, A) || ranges_overlap(C, B))
+    return fail(MMR_ERR_UNSAFE_ALIASING, "output storage overlaps an input");
+
+  const bool needs_bias = d->epilogue == MMR_EPI_BIAS || d->epilogue == MMR_EPI_BIAS_RELU;
+  if (needs_bias) {
+    const mmr_view& V = d->bias;
+    if ((rc = check_view(V, "bias", d->device_ordinal))) return rc;
+    if (V.rank != 1 || V.dims[0] != n)
+      return fail(MMR_ERR_INVALID_SHAPE, "bias must be rank 1 with N=%lld entries", (long long)n);
+    Operand bo;
+    set_range(bo, V);
+    if (ranges_overlap(C, bo)) return fail(MMR_ERR_UNSAFE_ALIASING, "output storage overlaps the bias");
+    p->bias = V.address + V.base_offset_bytes;
+    p->bias_s = V.strides[0];
+  }
+
+  p->batch0 = bdims[0];
+  p->batch1 = bdims[1];
+  p->m = m;
+  p->n = n;
+  p->k = k1;
+  p->a = A;
+  p->b = B;
+  p->c = C;
+  p->empty = (bdims[0] == 0 || bdims[1] == 0 || m == 0 || n == 0);
+  return MMR_OK;
+}
+
+// ---------------------------------------------------- family admission --
+
+// One batch axis for TMA: the operand is either broadcast over the whole
+// batch or indexed by the flattened batch index with a single stride.
+bool flat_batch(const Plan& p, const Operand& o, int64_t* stride, bool* batched) {
+  const int64_t b0 = p.batch0, b1 = p.batch1;
+  const bool v0 = b0 > 1 && o.s_b0 != 0, v1 = b1 > 1 && o.s_b1 != 0;
+  if (!v0 && !v1) {
+    *batched = false;
+    *stride = 0;
+    return (b0 <= 1 || o.s_b0 == 0) && (b1 <= 1 || o.s_b1 == 0);
+  }
+  *batched = true;
+  if (b0 <= 1) { *stride = o.s_b1; return true; }
+  if (b1 <= 1) { *stride = o.s_b0; return true; }
+  if (v0 && v1 && o.s_b0 == o.s_b1 * b1) { *stride = o.s_b1; return true; }
+  return false;
+}
+
+struct TmaLayout {
+  bool ok = false;
+  bool a_mn = false, b_mn = false;
+  bool a_batched = false, b_batched = false;
+  int64_t a_sb = 0, b_sb = 0, c_sb = 0;
+  const char* why = "";
+};
+
+TmaLayout tma_admission(const Plan& p) {
+  TmaLayout t;
+  auto aligned16 = [](uint64_t x) { return (x & 15u) == 0; };
+  if (p.k <= 0) { t.why = "K = 0"; return t; }
+  if (p.m > INT32_MAX || p.n > INT32_MAX || p.k > INT32_MAX) { t.why = "extent too large"; return t; }
+  bool cb;
+  if (!flat_batch(p, p.a, &t.a_sb, &t.a_batched) || !flat_batch(p, p.b, &t.b_sb, &t.b_batched) ||
+      !flat_batch(p, p.c, &t.c_sb, &cb)) {
+    t.why = "batch axes do not flatten to one strided axis";
+    return t;
+  }
+  const int64_t batch = p.batch0 * p.batch1;
+  if (batch > 1 && !cb) { t.why = "output broadcast over the batch"; return t; }
+  // A: K-contiguous (K-major) or M-contiguous (MN-major).
+  if (p.a.s_c == 1 && (p.a.s_r % 4 == 0) && p.a.s_r > 0) t.a_mn = false;
+  else if (p.a.s_r == 1 && (p.a.s_c % 4 == 0) && p.a.s_c > 0) t.a_mn = true;
+  else { t.why = "lhs has no unit-stride matrix axis with a 16-byte-aligned other stride"; return t; }
+  // B: N-contiguous (MN-major) or K-contiguous (K-major).
+  if (p.b.s_c == 1 && (p.b.s_r % 4 == 0) && p.b.s_r > 0) t.b_mn = true;
+  else if (p.b.s_r == 1 && (p.b.s_c % 4 == 0) && p.b.s_c > 0) t.b_mn = false;
+  else { t.why = "rhs has no unit-stride matrix axis with a 16-byte-aligned other stride"; return t; }
+  if (!(p.c.s_c == 1 && p.c.s_r % 4 == 0 && p.c.s_r > 0)) { t.why = "output is not row-major with 16-byte rows"; return t; }
+  if (!aligned16(p.a.base) || !aligned16(p.b.base) || !aligned16(p.c.base)) {
+    t.why = "operand base not 16-byte aligned";
+    return t;
+  }
+  if ((t.a_batched && t.a_sb % 4) || (t.b_batched && t.b_sb % 4) || (batch > 1 && t.c_sb % 4)) {
+    t.why = "batch stride not 16-byte aligned";
+    return t;
+  }
+  t.ok = true;
+  return t;
+}
+
+bool gemv_admission(const Plan& p, const char** why) {
+  if (p.batch0 * p.batch1 != 1) { *why = "batched"; return false; }
+  if (p.m < 1 || p.m > mmr::GV_MAX_M) { *why = "M outside 1..16"; return false; }
+  if (p.k < 1 || p.k > int64_t(mmr::GV_KSPLIT) * mmr::GV_MAX_KSLICE) { *why = "K outside 1..8192"; return false; }
+  if (!(p.b.s_c == 1 && p.b.s_r % 4 == 0 && (p.b.base & 15u) == 0 && p.n % 4 == 0)) {
+    *why = "rhs must be row-major with 16-byte rows and N % 4 == 0";
+    return false;
+  }
+  if (p.c.s_c != 1 && p.n > 1) { *why = "output columns not contiguous"; return false; }
+  if (p.bias && p.bias_s != 1) { *why = "strided bias"; return false; }
+  return true;
+}
+
+// --------------------------------------------------------- TMA encoding --
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 3-D f32 tensor map {inner, outer, batch} with 128-byte swizzle.
+int32_t encode_3d(CUtensorMap* tm, uint64_t base, uint64_t inner, uint64_t outer, uint64_t batch,
+                  int64_t outer_stride_el, int64_t batch_stride_el, uint32_t box_inner, uint32_t box_outer,
+                  const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(MMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if (batch < 1) batch = 1;
+  uint64_t bstride = uint64_t(batch_stride_el) * 4u;
+  if (batch == 1 || bstride == 0) {
+    // Unused axis (extent 1): any legal stride.
+    bstride = ((uint64_t(outer_stride_el) * 4u * std::max<uint64_t>(outer, 1)) + 15u) & ~uint64_t(15);
+    if (bstride == 0) bstride = 16;
+  }
+  cuuint64_t dims[3] = {inner, outer, batch};
+  cuuint64_t strides[2] = {uint64_t(outer_stride_el) * 4u, bstride};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, reinterpret_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: cuTensorMapEncodeTiled failed (%d): dims {%llu,%llu,%llu}", name,
+                int(r), (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)batch);
+  return MMR_OK;
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------- handle --
+
+struct mmr_gemm_handle {
+  Plan plan;
+  mmr_gemm_info info{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int family = MMR_FAMILY_AUTO;
+  // tcgen05
+  CUtensorMap tmA, tmB, tmC;
+  mmr::TcParams tcp{};
+  bool a_mn = false, b_mn = false;
+  int mode = 0;
+  // gemv
+  mmr::GemvParams gvp{};
+  int gv_mt = 16;
+  // simt
+  mmr::SimtParams sp{};
+  dim3 grid, block;
+  int smem = 0;
+  int* d_err = nullptr;
+  int* h_err = nullptr;  // pinned host copy of the error word
+  cudaEvent_t done = nullptr, err_ev = nullptr;
+  bool ran = false;
+  uint64_t wait_timeout_ns = 2000000000ull;
+};
+
+namespace {
+
+template <int MODE, bool AMN, bool BMN>
+cudaError_t launch_tc(mmr_gemm_handle* h, cudaStream_t s) {
+  mmr::tc_gemm_kernel<MODE, AMN, BMN><<<h->grid, h->block, h->smem, s>>>(h->tmA, h->tmB, h->tmC, h->tcp);
+  return cudaGetLastError();
+}
+
+template <int MODE, bool AMN, bool BMN>
+cudaError_t prepare_tc(int smem) {
+  return cudaFuncSetAttribute(mmr::tc_gemm_kernel<MODE, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              smem);
+}
+
+using TcLaunch = cudaError_t (*)(mmr_gemm_handle*, cudaStream_t);
+using TcPrep = cudaError_t (*)(int);
+
+TcLaunch tc_launch_table(int mode, bool amn, bool bmn) {
+  static const TcLaunch t[2][2][2] = {
+      {{launch_tc<0, false, false>, launch_tc<0, false, true>}, {launch_tc<0, true, false>, launch_tc<0, true, true>}},
+      {{launch_tc<1, false, false>, launch_tc<1, false, true>}, {launch_tc<1, true, false>, launch_tc<1, true, true>}}};
+  return t[mode][amn][bmn];
+}
+TcPrep tc_prep_table(int mode, bool amn, bool bmn) {
+  static const TcPrep t[2][2][2] = {
+      {{prepare_tc<0, false, false>, prepare_tc<0, false, true>}, {prepare_tc<0, true, false>, prepare_tc<0, true, true>}},
+      {{prepare_tc<1, false, false>, prepare_tc<1, false, true>}, {prepare_tc<1, true, false>, prepare_tc<1, true, true>}}};
+  return t[mode][amn][bmn];
+}
+
+template <int MT>
+cudaError_t launch_gemv_mt(const mmr_gemm_handle* h, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = h->grid;
+  cfg.blockDim = h->block;
+  cfg.dynamicSmemBytes = h->smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = mmr::GV_KSPLIT;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mmr::gemv_cluster_kernel<MT>, h->gvp);
+}
+
+template <int MT>
+cudaError_t prepare_gemv_mt(int smem) {
+  cudaError_t e = cudaFuncSetAttribute(mmr::gemv_cluster_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(mmr::gemv_cluster_kernel<MT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+}
+
+cudaError_t launch_gemv(const mmr_gemm_handle* h, cudaStream_t s) {
+  switch (h->gv_mt) {
+    case 1: return launch_gemv_mt<1>(h, s);
+    case 2: return launch_gemv_mt<2>(h, s);
+    case 4: return launch_gemv_mt<4>(h, s);
+    case 8: return launch_gemv_mt<8>(h, s);
+    default: return launch_gemv_mt<16>(h, s);
+  }
+}
+cudaError_t prepare_gemv(int mt, int smem) {
+  switch (mt) {
+    case 1: return prepare_gemv_mt<1>(smem);
+    case 2: return prepare_gemv_mt<2>(smem);
+    case 4: return prepare_gemv_mt<4>(smem);
+    case 8: return prepare_gemv_mt<8>(smem);
+    default: return prepare_gemv_mt<16>(smem);
+  }
+}
+
+void fill_info_common(const Plan& p, mmr_gemm_info* info) {
+  info->math_mode = p.math;
+  info->batch = p.batch0 * p.batch1;
+  info->m = p.m;
+  info->n = p.n;
+  info->k = p.k;
+  info->flops = 2.0 * double(info->batch) * double(p.m) * double(p.n) * double(p.k);
+}
+
+// Algorithmic HBM bytes: every operand element read once, C written once.
+double algorithmic_bytes(const Plan& p, bool a_batched, bool b_batched) {
+  const double batch = double(p.batch0 * p.batch1);
+  const double a = double(p.m) * double(p.k) * (a_batched ? batch : 1.0);
+  const double b = double(p.k) * double(p.n) * (b_batched ? batch : 1.0);
+  const double c = double(p.m) * double(p.n) * batch;
+  const double bias = p.bias ? double(p.n) : 0.0;
+  return 4.0 * (a + b + c + bias);
+}
+
+int32_t choose_family(const Plan& p, const TmaLayout& t, int32_t* family) {
+  const char* gemv_why = "";
+  const bool gemv_ok = p.math != MMR_MATH_EXACT && gemv_admission(p, &gemv_why);
+  if (p.family == MMR_FAMILY_AUTO) {
+    if (p.math == MMR_MATH_EXACT) *family = MMR_FAMILY_SIMT;
+    else if (gemv_ok) *family = MMR_FAMILY_GEMV;
+    else if (t.ok) *family = MMR_FAMILY_TCGEN05;
+    else *family = MMR_FAMILY_SIMT;
+    return MMR_OK;
+  }
+  if (p.family == MMR_FAMILY_TCGEN05) {
+    if (p.math == MMR_MATH_EXACT)
+      return fail(MMR_ERR_UNSUPPORTED_MATH, "the tcgen05 family cannot give the bit-exact reference order");
+    if (!t.ok) return fail(MMR_ERR_UNSUPPORTED_FAMILY, "tcgen05 family not admissible: %s", t.why);
+  } else if (p.family == MMR_FAMILY_GEMV) {
+    if (p.math == MMR_MATH_EXACT)
+      return fail(MMR_ERR_UNSUPPORTED_MATH, "the GEMV family splits K and cannot give the bit-exact order");
+    if (!gemv_ok) return fail(MMR_ERR_UNSUPPORTED_FAMILY, "GEMV family not admissible: %s", gemv_why);
+  }
+  *family = p.family;
+  return MMR_OK;
+}
+
+int32_t fill_validate_info(const Plan& p, mmr_gemm_info* info) {
+  TmaLayout t = tma_admission(p);
+  int32_t fam = MMR_FAMILY_AUTO;
+  int32_t rc = choose_family(p, t, &fam);
+  if (rc) return rc;
+  if (info) {
+    memset(info, 0, sizeof *info);
+    fill_info_common(p, info);
+    info->family = fam;
+    info->a_mn_major = t.a_mn;
+    info->b_mn_major = t.b_mn;
+    info->bytes = algorithmic_bytes(p, fam == MMR_FAMILY_TCGEN05 ? t.a_batched : true,
+                                    fam == MMR_FAMILY_TCGEN05 ? t.b_batched : true);
+  }
+  return MMR_OK;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------- ABI --
+
+extern "C" {
+
+const char* mmr_last_error(void) { return g_last_error.c_str(); }
+
+const char* mmr_version(void) {
+  return "momiru_b200 0.1.0 (sm_100a; tcgen05 tf32/3xtf32, gemv-cluster, simt-exact)";
+}
+
+int32_t mmr_gemm_validate(const mmr_matmul_desc* desc, mmr_gemm_info* info) {
+  Plan p;
+  int32_t rc = build_plan(desc, &p);
+  if (rc) return rc;
+  return fill_validate_info(p, info);
+}
+
+int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
+  if (!out) return fail(MMR_ERR_INVALID_ARGUMENT, "null output handle pointer");
+  *out = nullptr;
+  Plan p;
+  int32_t rc = build_plan(desc, &p);
+  if (rc) return rc;
+
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "no CUDA device is visible");
+  if (p.device < 0 || p.device >= ndev)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "device ordinal %d outside 0..%d", p.device, ndev - 1);
+  DeviceGuard guard(p.device);
+  if (!guard.ok) return fail(MMR_ERR_CUDA, "cudaSetDevice(%d) failed", p.device);
+  int major = 0, minor = 0, sms = 0;
+  MMR_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, p.device));
+  MMR_CUDA_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, p.device));
+  MMR_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, p.device));
+  if (major != 10 || minor != 0)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", p.device,
+                major, minor);
+  // Every bound address must be device memory of this ordinal.
+  const uint64_t addrs[4] = {desc->lhs.address, desc->rhs.address, desc->out.address,
+                             (desc->epilogue == MMR_EPI_BIAS || desc->epilogue == MMR_EPI_BIAS_RELU) ? desc->bias.address : 0};
+  for (uint64_t a : addrs) {
+    if (!a) continue;
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, reinterpret_cast<void*>(a)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(MMR_ERR_UNSUPPORTED_DEVICE, "address 0x%llx is not known to CUDA", (unsigned long long)a);
+    }
+    if (pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged)
+      return fail(MMR_ERR_UNSUPPORTED_DEVICE, "address 0x%llx is not device memory", (unsigned long long)a);
+    if (pa.device != p.device)
+      return fail(MMR_ERR_UNSUPPORTED_DEVICE, "address 0x%llx lives on device %d, not %d", (unsigned long long)a,
+                  pa.device, p.device);
+  }
+
+  TmaLayout t = tma_admission(p);
+  int32_t fam = MMR_FAMILY_AUTO;
+  if ((rc = choose_family(p, t, &fam))) return rc;
+
+  mmr_gemm_handle* h = new mmr_gemm_handle();
+  h->plan = p;
+  h->device = p.device;
+  h->stream = reinterpret_cast<cudaStream_t>(desc->stream);
+  h->family = fam;
+  fill_info_common(p, &h->info);
+  h->info.family = fam;
+
+  auto cleanup = [&](int32_t code) {
+    mmr_gemm_destroy(h);
+    return code;
+  };
+  if (cudaMalloc(&h->d_err, sizeof(int)) != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaMalloc(error word) failed"));
+  if (cudaMemset(h->d_err, 0, sizeof(int)) != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaMemset failed"));
+  if (cudaHostAlloc(&h->h_err, sizeof(int), cudaHostAllocDefault) != cudaSuccess)
+    return cleanup(fail(MMR_ERR_CUDA, "cudaHostAlloc failed"));
+  *h->h_err = 0;
+  if (cudaEventCreateWithFlags(&h->done, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&h->err_ev, cudaEventDisableTiming) != cudaSuccess)
+    return cleanup(fail(MMR_ERR_CUDA, "cudaEventCreate failed"));
+
+  if (p.empty) {
+    h->info.bytes = 0;
+    *out = h;
+    return MMR_OK;
+  }
+
+  const int64_t batch = p.batch0 * p.batch1;
+  if (fam == MMR_FAMILY_TCGEN05) {
+    h->mode = (p.math == MMR_MATH_STRICT_FP32) ? 1 : 0;
+    h->a_mn = t.a_mn;
+    h->b_mn = t.b_mn;
+    int32_t e;
+    // A
+    if (!t.a_mn) e = encode_3d(&h->tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, 32, mmr::TC_BM, "lhs");
+    else e = encode_3d(&h->tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, 32, "lhs");
+    if (e) return cleanup(e);
+    // B
+    if (t.b_mn) e = encode_3d(&h->tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, 32, "rhs");
+    else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, 32, mmr::TC_BN, "rhs");
+    if (e) return cleanup(e);
+    // C
+    e = encode_3d(&h->tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out");
+    if (e) return cleanup(e);
+
+    mmr::TcParams& q = h->tcp;
+    q.m = int(p.m);
+    q.n = int(p.n);
+    q.k = int(p.k);
+    q.batch = int(batch);
+    q.tiles_m = int((p.m + mmr::TC_BM - 1) / mmr::TC_BM);
+    q.tiles_n = int((p.n + mmr::TC_BN - 1) / mmr::TC_BN);
+    const int64_t tiles = int64_t(q.tiles_m) * q.tiles_n * batch;
+    if (tiles > INT32_MAX) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "too many output tiles"));
+    q.tiles_total = int(tiles);
+    q.k_blocks = int((p.k + mmr::TC_BK - 1) / mmr::TC_BK);
+    q.a_batched = t.a_batched;
+    q.b_batched = t.b_batched;
+    q.epilogue = p.epilogue;
+    q.bias = reinterpret_cast<const float*>(p.bias);
+    q.err = h->d_err;
+    q.timeout_ns = h->wait_timeout_ns;
+    h->smem = h->mode ? mmr::TcConfig<1>::kSmemBytes : mmr::TcConfig<0>::kSmemBytes;
+    h->grid = dim3(unsigned(std::min<int64_t>(tiles, sms)));
+    h->block = dim3(h->mode ? mmr::TcConfig<1>::kThreads : mmr::TcConfig<0>::kThreads);
+    cudaError_t ce = tc_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
+    if (ce != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce)));
+    h->info.a_mn_major = t.a_mn;
+    h->info.b_mn_major = t.b_mn;
+    h->info.tile_m = mmr::TC_BM;
+    h->info.tile_n = mmr::TC_BN;
+    h->info.tile_k = mmr::TC_BK;
+    h->info.stages = h->mode ? mmr::TcConfig<1>::kStages : mmr::TcConfig<0>::kStages;
+    h->info.tiles = tiles;
+    h->info.bytes = algorithmic_bytes(p, t.a_batched, t.b_batched);
+  } else if (fam == MMR_FAMILY_GEMV) {
+    mmr::GemvParams& g = h->gvp;
+    g.m = int(p.m);
+    g.n = int(p.n);
+    g.k = int(p.k);
+    int kslice = int((p.k + mmr::GV_KSPLIT - 1) / mmr::GV_KSPLIT);
+    kslice = (kslice + mmr::GV_WARPS - 1) / mmr::GV_WARPS * mmr::GV_WARPS;
+    g.kslice = kslice;
+    g.a = reinterpret_cast<const float*>(p.a.base);
+    g.a_m = p.a.s_r;
+    g.a_k = p.a.s_c;
+    g.b = reinterpret_cast<const float*>(p.b.base);
+    g.b_k = p.b.s_r;
+    g.c = reinterpret_cast<float*>(p.c.base);
+    g.c_m = p.c.s_r;
+    g.bias = reinterpret_cast<const float*>(p.bias);
+    g.epilogue = p.epilogue;
+    h->gv_mt = p.m <= 1 ? 1 : p.m <= 2 ? 2 : p.m <= 4 ? 4 : p.m <= 8 ? 8 : 16;
+    h->smem = mmr::gemv_smem_bytes(h->gv_mt, kslice);
+    h->grid = dim3(unsigned((p.n + mmr::GV_COLS - 1) / mmr::GV_COLS), mmr::GV_KSPLIT, 1);
+    h->block = dim3(mmr::GV_THREADS);
+    cudaError_t ce = prepare_gemv(h->gv_mt, h->smem);
+    if (ce != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaFuncSetAttribute(gemv): %s", cudaGetErrorString(ce)));
+    h->info.bytes = algorithmic_bytes(p, true, true);
+    h->info.cluster = mmr::GV_KSPLIT;
+  }
+  if (fam == MMR_FAMILY_SIMT) {
+    h->family = fam;
+    h->info.family = fam;
+    mmr::SimtParams& s = h->sp;
+    s.m = int(p.m);
+    s.n = int(p.n);
+    s.k = int(p.k);
+    s.batch0 = int(p.batch0);
+    s.batch1 = int(p.batch1);
+    s.a = reinterpret_cast<const float*>(p.a.base);
+    s.a_b0 = p.a.s_b0; s.a_b1 = p.a.s_b1; s.a_m = p.a.s_r; s.a_k = p.a.s_c;
+    s.b = reinterpret_cast<const float*>(p.b.base);
+    s.b_b0 = p.b.s_b0; s.b_b1 = p.b.s_b1; s.b_k = p.b.s_r; s.b_n = p.b.s_c;
+    s.c = reinterpret_cast<float*>(p.c.base);
+    s.c_b0 = p.c.s_b0; s.c_b1 = p.c.s_b1; s.c_m = p.c.s_r; s.c_n = p.c.s_c;
+    s.bias = reinterpret_cast<const float*>(p.bias);
+    s.bias_n = p.bias_s;
+    s.epilogue = p.epilogue;
+    if (batch > 65535) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "batch too large for the SIMT family"));
+    h->grid = dim3(unsigned((p.n + mmr::SIMT_BN - 1) / mmr::SIMT_BN), unsigned((p.m + mmr::SIMT_BM - 1) / mmr::SIMT_BM),
+                   unsigned(batch));
+    if (h->grid.y > 65535) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "M too large for the SIMT family"));
+    h->block = dim3(256);
+    h->smem = 0;
+    h->info.bytes = algorithmic_bytes(p, true, true);
+  }
+  h->info.grid = int(h->grid.x * h->grid.y * h->grid.z);
+  h->info.block = int(h->block.x);
+  h->info.smem_bytes = h->smem;
+  *out = h;
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
+  if (!h) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  DeviceGuard guard(h->device);
+  if (!guard.ok) return fail(MMR_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+  cudaError_t e = cudaSuccess;
+  if (!h->plan.empty) {
+    switch (h->family) {
+      case MMR_FAMILY_TCGEN05: e = tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s); break;
+      case MMR_FAMILY_GEMV: e = launch_gemv(h, s); break;
+      case MMR_FAMILY_SIMT:
+        mmr::simt_gemm_exact_kernel<<<h->grid, h->block, 0, s>>>(h->sp);
+        e = cudaGetLastError();
+        break;
+      default: return fail(MMR_ERR_UNSUPPORTED_FAMILY, "no kernel bound");
+    }
+  }
+  if (e != cudaSuccess) return fail(MMR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  MMR_CUDA_TRY(cudaEventRecord(h->done, s));
+  h->ran = true;
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_run(mmr_gemm_handle* h) {
+  if (!h) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle");
+  return mmr_gemm_run_on(h, h->stream);
+}
+
+static int32_t poll_event(cudaEvent_t ev, uint64_t timeout_ns) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaEventQuery(ev);
+    if (e == cudaSuccess) return MMR_OK;
+    if (e != cudaErrorNotReady) return fail(MMR_ERR_CUDA, "cudaEventQuery: %s", cudaGetErrorString(e));
+    const uint64_t el = uint64_t(std::chrono::duration_cast<std::chrono::nanoseconds>(
+                                     std::chrono::steady_clock::now() - t0)
+                                     .count());
+    if (el > timeout_ns) return fail(MMR_ERR_TIMEOUT, "work did not complete within %llu ns", (unsigned long long)timeout_ns);
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+int32_t mmr_gemm_quiesce(mmr_gemm_handle* h, uint64_t timeout_ns) {
+  if (!h) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle");
+  if (!h->ran) return MMR_OK;
+  DeviceGuard guard(h->device);
+  int32_t rc = poll_event(h->done, timeout_ns);
+  if (rc) return rc;
+  // Read the device error word (asynchronously, then poll: never block forever).
+  MMR_CUDA_TRY(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+  MMR_CUDA_TRY(cudaEventRecord(h->err_ev, h->stream));
+  if ((rc = poll_event(h->err_ev, timeout_ns))) return rc;
+  const int code = *h->h_err;
+  if (code != 0) {
+    *h->h_err = 0;
+    cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
+    return fail(code == mmr::kDevTimeoutDrain || code <= mmr::kDevTimeoutXform ? MMR_ERR_TIMEOUT
+                                                                               : MMR_ERR_DEVICE_FAULT_FLAG,
+                "kernel reported device error word %d (a bounded wait expired)", code);
+  }
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_destroy(mmr_gemm_handle* h) {
+  if (!h) return MMR_OK;
+  int32_t rc = MMR_OK;
+  {
+    DeviceGuard guard(h->device);
+    if (h->ran && h->done) rc = poll_event(h->done, 10000000000ull);
+    if (h->done) cudaEventDestroy(h->done);
+    if (h->err_ev) cudaEventDestroy(h->err_ev);
+    if (h->d_err) cudaFree(h->d_err);
+    if (h->h_err) cudaFreeHost(h->h_err);
+  }
+  delete h;
+  return rc;
+}
+
+namespace {
+__global__ void bounded_wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mmr::mbar_init(&bar, 1);
+    mmr::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Nobody arrives: the wait must expire, record the code and return.
+    const mmr::WaitCtl ctl{err, limit_ns};
+    mmr::mbar_wait(&bar, 0u, ctl, mmr::kDevTimeoutProbe);
+  }
+  __syncthreads();
+}
+}  // namespace
+
+int32_t mmr_selftest_bounded_wait(int32_t device_ordinal, uint64_t limit_ns) {
+  DeviceGuard guard(device_ordinal);
+  if (!guard.ok) return fail(MMR_ERR_CUDA, "cudaSetDevice(%d) failed", device_ordinal);
+  if (limit_ns > 5000000000ull) return fail(MMR_ERR_INVALID_ARGUMENT, "limit above 5 s");
+  int* d_err = nullptr;
+  MMR_CUDA_TRY(cudaMalloc(&d_err, sizeof(int)));
+  int h = -1;
+  cudaError_t e = cudaMemset(d_err, 0, sizeof(int));
+  if (e == cudaSuccess) {
+    bounded_wait_probe_kernel<<<1, 32>>>(d_err, limit_ns);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(d_err);
+  if (e != cudaSuccess) return fail(MMR_ERR_CUDA, "bounded-wait probe: %s", cudaGetErrorString(e));
+  if (h == mmr::kDevTimeoutProbe) return fail(MMR_ERR_TIMEOUT, "probe wait expired as designed");
+  return fail(MMR_ERR_DEVICE_FAULT_FLAG, "probe returned error word %d", h);
+}
+
+int32_t mmr_shard_columns(int64_t n, int32_t nranks, int32_t rank, int32_t align, int64_t* col0, int64_t* col1) {
+  if (!col0 || !col1 || nranks < 1 || rank < 0 || rank >= nranks || n < 0 || align < 1)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "bad shard request");
+  // Whole `align`-column units are dealt out as evenly as possible; the first
+  // (units % nranks) ranks take one extra unit. The last rank absorbs the tail.
+  const int64_t units = (n + align - 1) / align;
+  const int64_t base = units / nranks, extra = units % nranks;
+  const int64_t u0 = rank * base + std::min<int64_t>(rank, extra);
+  const int64_t u1 = u0 + base + (rank < extra ? 1 : 0);
+  *col0 = std::min<int64_t>(n, u0 * align);
+  *col1 = std::min<int64_t>(n, u1 * align);
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_query(const mmr_gemm_handle* h, mmr_gemm_info* info) {
+  if (!h || !info) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle or info");
+  *info = h->info;
+  return MMR_OK;
+}
+
+}  // extern "C"

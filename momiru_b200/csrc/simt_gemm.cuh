@@ -1,0 +1,90 @@
+// simt_gemm.cuh -- CUDA-core f32 GEMM in the reference's exact arithmetic.
+//
+// Every output element is s = +0; for p = 0..K-1: s = s + (a*b), with the
+// product and the sum each rounded to f32 (__fmul_rn / __fadd_rn, no FMA) and
+// p increasing -- the per-element order of gemm_dot_f32 / gemm_axpy_f32 /
+// gemm_avx2 (src/momiru/tensor_light/execution/cpu.rs:2989-3098). Results are
+// therefore bit-identical to the reference except for NaN payloads. Handles any
+// non-negative element strides, up to two batch axes with broadcast (stride 0),
+// K = 0 (+0 then the epilogue), and every shape. It serves MMR_MATH_EXACT and
+// the layouts TMA cannot describe.
+#pragma once
+#include <stdint.h>
+
+namespace mmr {
+
+struct SimtParams {
+  int m, n, k;
+  int batch0, batch1;
+  const float* a; long long a_b0, a_b1, a_m, a_k;
+  const float* b; long long b_b0, b_b1, b_k, b_n;
+  float* c; long long c_b0, c_b1, c_m, c_n;
+  const float* bias; long long bias_n;
+  int epilogue;  // 0 none, 1 bias, 2 bias+relu, 3 relu
+};
+
+constexpr int SIMT_BM = 64, SIMT_BN = 64, SIMT_BK = 16;
+
+__global__ void __launch_bounds__(256) simt_gemm_exact_kernel(const SimtParams p) {
+  __shared__ float As[SIMT_BK][SIMT_BM + 4];
+  __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int n0 = blockIdx.x * SIMT_BN, m0 = blockIdx.y * SIMT_BM;
+  const int bz = blockIdx.z;
+  const int b0 = bz / p.batch1, b1 = bz - (bz / p.batch1) * p.batch1;
+  const float* A = p.a + b0 * p.a_b0 + b1 * p.a_b1;
+  const float* B = p.b + b0 * p.b_b0 + b1 * p.b_b1;
+  float* C = p.c + b0 * p.c_b0 + b1 * p.c_b1;
+
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+
+  for (int k0 = 0; k0 < p.k; k0 += SIMT_BK) {
+    const int kmax = min(SIMT_BK, p.k - k0);
+    for (int idx = threadIdx.x; idx < SIMT_BK * SIMT_BM; idx += 256) {
+      const int kk = idx / SIMT_BM, mm = idx - kk * SIMT_BM;
+      const int gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < p.m && kk < kmax) ? A[gm * p.a_m + gk * p.a_k] : 0.0f;
+    }
+    for (int idx = threadIdx.x; idx < SIMT_BK * SIMT_BN; idx += 256) {
+      const int kk = idx / SIMT_BN, nn = idx - kk * SIMT_BN;
+      const int gn = n0 + nn, gk = k0 + kk;
+      Bs[kk][nn] = (gn < p.n && kk < kmax) ? B[gk * p.b_k + gn * p.b_n] : 0.0f;
+    }
+    __syncthreads();
+    for (int kk = 0; kk < kmax; ++kk) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(av[i], bv[j]));
+    }
+    __syncthreads();
+  }
+
+  const bool add_bias = (p.epilogue == 1 || p.epilogue == 2);
+  const bool relu = (p.epilogue == 2 || p.epilogue == 3);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int gm = m0 + ty * 4 + i;
+    if (gm >= p.m) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gn = n0 + tx * 4 + j;
+      if (gn >= p.n) continue;
+      float x = acc[i][j];
+      if (add_bias) x = __fadd_rn(x, p.bias[gn * p.bias_n]);
+      if (relu) x = (x != x) ? x : (x > 0.0f ? x : 0.0f);
+      C[gm * p.c_m + gn * p.c_n] = x;
+    }
+  }
+}
+
+}  // namespace mmr

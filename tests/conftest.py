@@ -1,0 +1,28 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+@pytest.fixture(scope="session")
+def oracle():
+    from oracle import oracle as O
+    O.build()
+    assert O.selfcheck_kat() == 0
+    return O
+
+
+@pytest.fixture(scope="session")
+def cuda_lib():
+    from momiru_b200 import build
+    build.build()
+    from momiru_b200 import _abi
+    return _abi.load()

@@ -1,0 +1,173 @@
+"""The C ABI on the host: the library loads, exports every declared symbol,
+and its bind-time contract (validation.rs:2300-2398 shape/broadcast rules,
+layout admission, aliasing, math contract, family choice) behaves as the
+reference's validator does. No GPU: mmr_gemm_validate touches no device."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+from momiru_b200 import (AccuracyContract, Epilogue, KernelFamily, KernelMathMode, MatMulNode, PlanError, validate)
+from momiru_b200 import _abi, execution
+from momiru_b200.tensor import DeviceBuffer, DeviceView
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+G = 1 << 36
+
+
+def fake(dims, slot, pad_cols=None):
+    """A contiguous view over a fake device address (never dereferenced)."""
+    dims = tuple(dims)
+    if pad_cols:
+        phys = dims[:-1] + (pad_cols,)
+        buf = DeviceBuffer(slot * G, 4 * int(np.prod(phys)), 0)
+        return DeviceView.contiguous(buf, phys).narrow(-1, 0, dims[-1])
+    return DeviceView.contiguous(DeviceBuffer(slot * G, 4 * max(1, int(np.prod(dims))), 0), dims)
+
+
+def test_library_exports_every_declared_symbol(cuda_lib):
+    header = open(os.path.join(ROOT, "include", "momiru_gemm.h")).read()
+    declared = set(re.findall(r"MMR_API\s+(?:int32_t|const char \*)\s*(mmr_\w+)\s*\(", header))
+    assert declared, "no declarations parsed"
+    assert declared == set(_abi.EXPORTED)
+    for name in declared:
+        assert hasattr(cuda_lib, name), name
+    assert b"sm_100a" in cuda_lib.mmr_version()
+
+
+def test_configs_pick_expected_families():
+    # C1 512^3
+    assert validate(MatMulNode(), fake((512, 512), 1), fake((512, 512), 2), fake((512, 512), 3))["family"] == 1
+    # C2 batched with B broadcast
+    info = validate(MatMulNode(), fake((64, 256, 256), 1), fake((256, 256), 2), fake((64, 256, 256), 3))
+    assert info["family"] == 1 and info["batch"] == 64 and info["bytes"] == 4 * (64 * 256 * 256 * 2 + 256 * 256)
+    # C3 with fused bias+ReLU
+    n = MatMulNode(epilogue=Epilogue.BIAS_RELU)
+    info = validate(n, fake((8192, 8192), 1), fake((8192, 8192), 2), fake((8192, 8192), 3), fake((8192,), 4))
+    assert info["family"] == 1 and info["flops"] == 2 * 8192 ** 3
+    # C4 zero-copy strided views
+    x, w = fake((4096, 4096), 1), fake((4096, 12288), 2)
+    info = validate(MatMulNode(), x.transpose(), w.narrow(1, 0, 11008), fake((4096, 11008), 3))
+    assert info["family"] == 1 and info["a_mn_major"] == 1 and info["b_mn_major"] == 1
+    # the same via the node's transpose flag on the physical buffer
+    info = validate(MatMulNode(transpose_lhs=True), x, w.narrow(1, 0, 11008), fake((4096, 11008), 3))
+    assert info["family"] == 1 and info["a_mn_major"] == 1
+    # C5a
+    assert validate(MatMulNode(), fake((512, 1024, 1024), 1), fake((512, 1024, 1024), 2),
+                    fake((512, 1024, 1024), 3))["batch"] == 512
+    # C5b -> GEMV
+    for m in (1, 4, 16):
+        assert validate(MatMulNode(), fake((m, 4096), 1), fake((4096, 4096), 2), fake((m, 4096), 3))["family"] == 2
+    # Exact always runs the reference order on CUDA cores
+    assert validate(MatMulNode(math_mode=KernelMathMode.Exact), fake((512, 512), 1), fake((512, 512), 2),
+                    fake((512, 512), 3))["family"] == 3
+
+
+def test_unaligned_layouts_fall_back_to_simt_or_reject_forced_family():
+    a, b, c = fake((5, 7), 1), fake((7, 3), 2), fake((5, 3), 3)
+    assert validate(MatMulNode(), a, b, c)["family"] == 3
+    with pytest.raises(execution.UnsupportedFamily):
+        validate(MatMulNode(family=KernelFamily.Tcgen05), a, b, c)
+    with pytest.raises(execution.InvalidAccuracyContract):
+        validate(MatMulNode(math_mode=KernelMathMode.Exact, family=KernelFamily.Gemv), a, b, c)
+    # padded rows make the same logical shapes TMA-admissible
+    a, b, c = fake((5, 7), 1, pad_cols=8), fake((7, 3), 2, pad_cols=4), fake((5, 3), 3, pad_cols=4)
+    # N = 3 is not a whole float4 so GEMV declines; TMA clips the ragged tile
+    assert validate(MatMulNode(), a, b, c)["family"] == 1
+    with pytest.raises(execution.UnsupportedFamily):
+        validate(MatMulNode(family=KernelFamily.Gemv), a, b, c)
+
+
+@pytest.mark.parametrize("lhs,rhs,out,ok", [
+    ((3, 4), (4, 5), (3, 5), True),
+    ((4,), (4, 5), (5,), True),              # rank-1 lhs: promoted dim removed
+    ((3, 4), (4,), (3,), True),              # rank-1 rhs
+    ((4,), (4,), (1,), True),                # dot -> scalar (held as [1])
+    ((2, 3, 4), (4, 5), (2, 3, 5), True),    # broadcast rhs
+    ((1, 3, 4), (6, 4, 5), (6, 3, 5), True),  # 1 vs 6 -> 6
+    ((0, 3, 4), (1, 4, 5), (0, 3, 5), True),  # 0 vs 1 -> 0 (not max)
+    ((2, 3, 4), (3, 4, 5), (2, 3, 5), False),  # 2 vs 3
+    ((3, 4), (5, 6), (3, 6), False),         # K mismatch
+    ((3, 4), (4, 5), (3, 6), False),         # wrong N
+    ((3, 4), (4, 5), (1, 3, 5), False),      # wrong rank
+])
+def test_shape_contract(lhs, rhs, out, ok):
+    args = (MatMulNode(), fake(lhs, 1), fake(rhs, 2), fake(out, 3))
+    if ok:
+        validate(*args)
+    else:
+        with pytest.raises(execution.InvalidShape):
+            validate(*args)
+
+
+def test_transpose_flags_and_rank1():
+    validate(MatMulNode(transpose_lhs=True, transpose_rhs=True), fake((4, 3), 1), fake((5, 4), 2), fake((3, 5), 3))
+    with pytest.raises(execution.InvalidShape):
+        validate(MatMulNode(transpose_lhs=True), fake((4,), 1), fake((4, 5), 2), fake((5,), 3))
+
+
+def test_aliasing_bounds_alignment_device():
+    a = fake((64, 64), 1)
+    with pytest.raises(execution.UnsafeAliasing):
+        validate(MatMulNode(), a, fake((64, 64), 2), a)
+    # an output view inside the rhs buffer
+    big = fake((64, 128), 2)
+    with pytest.raises(execution.UnsafeAliasing):
+        validate(MatMulNode(), a, big.narrow(1, 0, 64), big.narrow(1, 64, 64))
+    # view larger than its buffer
+    buf = DeviceBuffer(5 * G, 4 * 100, 0)
+    v = DeviceView(buf, (10, 11), (11, 1), 0)
+    with pytest.raises(execution.OutOfBounds):
+        validate(MatMulNode(), v, fake((11, 3), 2), fake((10, 3), 3))
+    # misaligned base offset (bytes not a multiple of 4 cannot be expressed by
+    # element offsets, so use a raw ABI descriptor)
+    d = execution._desc(MatMulNode(), a, fake((64, 64), 2), fake((64, 64), 3), None, None)
+    d.lhs.base_offset_bytes = 2
+    info = _abi.MmrGemmInfo()
+    import ctypes
+    assert _abi.load().mmr_gemm_validate(ctypes.byref(d), ctypes.byref(info)) == _abi.ERR_UNSUPPORTED_LAYOUT
+    # device ordinal mismatch
+    other = DeviceView.contiguous(DeviceBuffer(6 * G, 4 * 64 * 64, 1), (64, 64))
+    with pytest.raises(execution.UnsupportedDevice):
+        validate(MatMulNode(), a, other, fake((64, 64), 3))
+    # negative strides are not admitted
+    neg = DeviceView(DeviceBuffer(7 * G, 4 * 64 * 64, 0), (64, 64), (64, -1), 63)
+    with pytest.raises(execution.UnsupportedLayout):
+        validate(MatMulNode(), a, neg, fake((64, 64), 3))
+
+
+def test_bias_contract():
+    n = MatMulNode(epilogue=Epilogue.BIAS)
+    validate(n, fake((8, 4), 1), fake((4, 16), 2), fake((8, 16), 3), fake((16,), 4))
+    with pytest.raises(execution.InvalidShape):
+        validate(n, fake((8, 4), 1), fake((4, 16), 2), fake((8, 16), 3), fake((8,), 4))
+
+
+def test_math_contract_mirrors_reference():
+    # validation.rs:3579-3640
+    MatMulNode(math_mode=KernelMathMode.Tf32, accuracy=AccuracyContract.AllowTf32)
+    MatMulNode(math_mode=KernelMathMode.StrictFp32, accuracy=AccuracyContract.AllowTf32)
+    MatMulNode(math_mode=KernelMathMode.Exact, accuracy=AccuracyContract.Exact)
+    with pytest.raises(PlanError):
+        MatMulNode(math_mode=KernelMathMode.Tf32, accuracy=AccuracyContract.StrictFp32)
+    with pytest.raises(PlanError):
+        MatMulNode(math_mode=KernelMathMode.StrictFp32, accuracy=AccuracyContract.Exact)
+
+
+def test_output_dims_helper():
+    from momiru_b200 import output_dims
+    assert output_dims(MatMulNode(), fake((2, 3, 4), 1), fake((4, 5), 2)) == (2, 3, 5)
+    assert output_dims(MatMulNode(transpose_lhs=True), fake((4, 3), 1), fake((4, 5), 2)) == (3, 5)
+    assert output_dims(MatMulNode(), fake((4,), 1), fake((4,), 2)) == ()
+
+
+def test_view_ops():
+    v = fake((4, 6), 1)
+    t = v.transpose()
+    assert t.dims == (6, 4) and t.strides == (1, 6)
+    n = v.narrow(1, 2, 3)
+    assert n.dims == (4, 3) and n.offset == 2
+    s = v.slice([(1, 4, 2), None])
+    assert s.dims == (2, 6) and s.strides == (12, 1) and s.offset == 6
+    assert v.is_row_major_contiguous() and not t.is_row_major_contiguous()

@@ -1,0 +1,361 @@
+"""GPU parity of the f32 matmul hot path against the CPU oracle, through the C ABI.
+
+Tolerances (relative Frobenius error against the oracle, the restated
+reference CPU GEMM):
+  StrictFp32 (3xTF32 on tcgen05, and the GEMV family)   <= 1e-5
+  Tf32 (one TF32 pass)                                  <= 2e-3
+  Exact (CUDA-core kernel in the reference's order)     bit-identical
+"""
+import numpy as np
+import pytest
+
+from momiru_b200 import (BoundGemm, DeviceBuffer, DeviceView, Epilogue, KernelFamily, KernelMathMode, MatMulNode,
+                         PlanError, matmul, selftest_bounded_wait)
+from momiru_b200 import _abi, execution
+from momiru_b200 import rng
+
+pytestmark = pytest.mark.gpu
+
+STRICT_TOL = 1e-5
+TF32_TOL = 2e-3
+STRICT = MatMulNode(math_mode=KernelMathMode.StrictFp32)
+TF32 = MatMulNode(math_mode=KernelMathMode.Tf32, accuracy=execution.AccuracyContract.AllowTf32)
+EXACT = MatMulNode(math_mode=KernelMathMode.Exact, accuracy=execution.AccuracyContract.Exact)
+
+
+def rel_frob(x, ref):
+    x = np.asarray(x, np.float64)
+    ref = np.asarray(ref, np.float64)
+    den = np.linalg.norm(ref)
+    return float(np.linalg.norm(x - ref) / (den if den > 0 else 1.0))
+
+
+def node(base, **kw):
+    d = dict(transpose_lhs=base.transpose_lhs, transpose_rhs=base.transpose_rhs, math_mode=base.math_mode,
+             epilogue=base.epilogue, family=base.family, accuracy=base.accuracy)
+    d.update(kw)
+    return MatMulNode(**d)
+
+
+def padded(arr, pad_to=4):
+    """Device copy of a 2-D/3-D array whose rows are padded to a multiple of
+    `pad_to` elements, returned as the narrowed (logical) view."""
+    arr = np.ascontiguousarray(arr, np.float32)
+    cols = arr.shape[-1]
+    pc = (cols + pad_to - 1) // pad_to * pad_to
+    phys = np.zeros(arr.shape[:-1] + (pc,), np.float32)
+    phys[..., :cols] = arr
+    v = DeviceView.from_host(phys)
+    return v.narrow(-1, 0, cols)
+
+
+def run(node_, a, b, bias=None, out_dims=None, family=None):
+    """Bind, replay once, quiesce; the output rows are padded to 16 bytes."""
+    if family is not None:
+        node_ = node(node_, family=family)
+    dims = out_dims or execution.output_dims(node_, a, b)
+    out = padded(np.zeros(dims, np.float32)) if len(dims) >= 2 else DeviceView.empty(dims)
+    with BoundGemm(node_, a, b, out, bias) as g:
+        g.replay()
+        g.quiesce_or_abort(60)
+        fam = g.family
+    return out.to_host(), fam
+
+
+# ----------------------------------------------------------------- basics --
+def test_bounded_wait_probe_returns_timeout_and_context_survives():
+    assert selftest_bounded_wait(0, 0.02) == _abi.ERR_TIMEOUT
+    a = DeviceView.from_host(np.eye(4, dtype=np.float32))
+    out = matmul(a, a, node=EXACT)
+    assert np.array_equal(out.to_host(), np.eye(4, dtype=np.float32))
+
+
+@pytest.mark.parametrize("fam,mode", [(KernelFamily.Tcgen05, STRICT), (KernelFamily.Tcgen05, TF32),
+                                      (KernelFamily.Simt, EXACT), (KernelFamily.Gemv, STRICT),
+                                      (KernelFamily.Auto, STRICT)])
+def test_reference_kat_every_family(oracle, fam, mode):
+    # cpu.rs:827-846: [[1,2,3],[4,5,6]] @ [[7,8],[9,10],[11,12]] = [[58,64],[139,154]]
+    a = np.array([[1, 2, 3], [4, 5, 6]], np.float32)
+    b = np.array([[7, 8], [9, 10], [11, 12]], np.float32)
+    want = np.array([[58, 64], [139, 154]], np.float32)
+    if fam == KernelFamily.Gemv:
+        b4 = np.zeros((3, 4), np.float32)
+        b4[:, :2] = b
+        got, f = run(mode, padded(a), DeviceView.from_host(b4), out_dims=(2, 4), family=fam)
+        got = got[:, :2]
+    else:
+        got, f = run(mode, padded(a), padded(b), family=fam)
+    assert np.array_equal(got, want), (f, got)
+
+
+# ---------------------------------------------------------------- C1 512^3 --
+@pytest.mark.parametrize("mode,tol", [(STRICT, STRICT_TOL), (TF32, TF32_TOL)])
+def test_c1_square_512(oracle, mode, tol):
+    a = rng.randu((512, 512), 1)
+    b = rng.randu((512, 512), 2)
+    ref = oracle.matmul(a, b)
+    got, fam = run(mode, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert fam == "tcgen05"
+    assert rel_frob(got, ref) <= tol
+
+
+def test_c1_exact_is_bit_identical(oracle):
+    a = rng.randu((512, 512), 1)
+    b = rng.randu((512, 512), 2)
+    ref = oracle.matmul(a, b)
+    got, fam = run(EXACT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert fam == "simt"
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_repeat_runs_are_bitwise_deterministic():
+    a = DeviceView.from_host(rng.randu((384, 640), 3))
+    b = DeviceView.from_host(rng.randu((640, 520), 4))
+    out = DeviceView.empty((384, 520))
+    with BoundGemm(STRICT, a, b, out) as g:
+        g.replay()
+        g.quiesce_or_abort()
+        first = out.to_host()
+        for _ in range(3):
+            g.replay()
+        g.quiesce_or_abort()
+    assert np.array_equal(first.view(np.uint32), out.to_host().view(np.uint32))
+
+
+# ------------------------------------------------- C2 batched + broadcast --
+def test_c2_batched_broadcast(oracle):
+    a = rng.randn((64, 256, 256), 1)
+    b = rng.randn((256, 256), 2)
+    ref = oracle.matmul(a, b)
+    da, db = DeviceView.from_host(a), DeviceView.from_host(b)
+    got, fam = run(STRICT, da, db)
+    assert fam == "tcgen05" and rel_frob(got, ref) <= STRICT_TOL
+    got, _ = run(TF32, da, db)
+    assert rel_frob(got, ref) <= TF32_TOL
+    got, fam = run(EXACT, da, db)
+    assert fam == "simt" and np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_batched_broadcast_lhs_and_two_batch_axes(oracle):
+    a = rng.randn((256, 64), 5)
+    b = rng.randn((3, 64, 96), 6)
+    ref = np.stack([oracle.matmul(a, b[i]) for i in range(3)])
+    got, fam = run(STRICT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert fam == "tcgen05" and rel_frob(got, ref) <= STRICT_TOL
+    # [2,1,M,K] x [1,3,K,N] -> [2,3,M,N] cannot flatten to one batch axis: SIMT
+    a4 = rng.randn((2, 1, 40, 24), 7)
+    b4 = rng.randn((1, 3, 24, 36), 8)
+    ref4 = np.stack([np.stack([oracle.matmul(a4[i, 0], b4[0, j]) for j in range(3)]) for i in range(2)])
+    got4, fam = run(EXACT, DeviceView.from_host(a4), DeviceView.from_host(b4))
+    assert np.array_equal(got4.view(np.uint32), ref4.view(np.uint32))
+
+
+# ------------------------------------------------------ C3 fused epilogue --
+@pytest.mark.parametrize("mode,tol", [(STRICT, STRICT_TOL), (TF32, TF32_TOL)])
+@pytest.mark.parametrize("epi", [Epilogue.BIAS_RELU, Epilogue.BIAS, Epilogue.RELU])
+def test_c3_epilogue_1024(oracle, mode, tol, epi):
+    a = rng.randu((1024, 1024), 1)
+    b = rng.randu((1024, 1024), 2)
+    bias = rng.randn((1024,), 3, 0.1)
+    oepi = {Epilogue.BIAS_RELU: oracle.EPI_BIAS_RELU, Epilogue.BIAS: oracle.EPI_BIAS, Epilogue.RELU: oracle.EPI_RELU}[epi]
+    ref = oracle.matmul(a, b, bias=bias, epilogue=oepi)
+    got, fam = run(node(mode, epilogue=epi), DeviceView.from_host(a), DeviceView.from_host(b),
+                   DeviceView.from_host(bias))
+    assert fam == "tcgen05" and rel_frob(got, ref) <= tol
+    if epi != Epilogue.BIAS:
+        # ReLU writes +0 (never -0) wherever the reference does.
+        zeros = ref == 0
+        assert np.all(got.view(np.uint32)[zeros & (got == 0)] == 0)
+        assert not np.any(np.signbit(got))
+
+
+def test_c3_full_size_row_sampled(oracle):
+    """8192^3 + bias + ReLU: all rows computed on the GPU, 48 rows checked
+    against the oracle, and a size-independent column-sum identity checked on
+    the pre-activation product."""
+    n = 8192
+    a = rng.randu((n, n), 1)
+    b = rng.randu((n, n), 2)
+    bias = rng.randn((n,), 3, 0.1)
+    da, db, dbias = DeviceView.from_host(a), DeviceView.from_host(b), DeviceView.from_host(bias)
+    rows = np.random.default_rng(0).choice(n, 48, replace=False)
+    ref = oracle.matmul(a, b, bias=bias, epilogue=oracle.EPI_BIAS_RELU, rows=rows)
+    for mode, tol in ((STRICT, STRICT_TOL), (TF32, TF32_TOL)):
+        got, fam = run(node(mode, epilogue=Epilogue.BIAS_RELU), da, db, dbias)
+        assert fam == "tcgen05"
+        assert np.isfinite(got).all()
+        assert rel_frob(got[rows], ref) <= tol, mode
+    # column sums: 1^T (A B) == (1^T A) B, in f64 on the host
+    plain, _ = run(STRICT, da, db)
+    lhs = plain.astype(np.float64).sum(axis=0)
+    rhs = a.astype(np.float64).sum(axis=0) @ b.astype(np.float64)
+    assert rel_frob(lhs, rhs) <= 1e-6
+
+
+# ----------------------------------------------------- C4 strided views --
+def _c4(oracle, m, k, n, n_phys, rows=None):
+    x = rng.randn((k, m), 1, 0.02)          # A = X^T
+    w = rng.randn((k, n_phys), 2, 0.02)     # B = W[:, :n]
+    dx, dw = DeviceView.from_host(x), DeviceView.from_host(w)
+    ref = oracle.matmul(x.T, w[:, :n], rows=rows)
+    return dx, dw, ref
+
+
+def test_c4_strided_views_reduced(oracle):
+    dx, dw, ref = _c4(oracle, 1024, 1024, 2752, 3072)
+    for view_form in ("view", "flag"):
+        lhs = dx.transpose() if view_form == "view" else dx
+        nd = STRICT if view_form == "view" else node(STRICT, transpose_lhs=True)
+        got, fam = run(nd, lhs, dw.narrow(1, 0, 2752))
+        assert fam == "tcgen05" and rel_frob(got, ref) <= STRICT_TOL
+    got, _ = run(TF32, dx.transpose(), dw.narrow(1, 0, 2752))
+    assert rel_frob(got, ref) <= TF32_TOL
+
+
+def test_c4_full_size_row_sampled(oracle):
+    rows = np.random.default_rng(1).choice(4096, 32, replace=False)
+    dx, dw, ref = _c4(oracle, 4096, 4096, 11008, 12288, rows=rows)
+    got, fam = run(STRICT, dx.transpose(), dw.narrow(1, 0, 11008))
+    assert fam == "tcgen05" and rel_frob(got[rows], ref) <= STRICT_TOL
+
+
+def test_k_major_rhs_via_transpose_flag(oracle):
+    a = rng.randn((300, 200), 1)
+    bt = rng.randn((260, 200), 2)           # B^T stored [N, K]
+    ref = oracle.matmul(a, bt.T)
+    got, fam = run(node(STRICT, transpose_rhs=True), DeviceView.from_host(a), DeviceView.from_host(bt))
+    assert fam == "tcgen05" and rel_frob(got, ref) <= STRICT_TOL
+
+
+# ------------------------------------------------------- C5a big batches --
+def test_c5a_batched_reduced(oracle):
+    a = rng.randu((8, 1024, 1024), 1)
+    b = rng.randu((8, 1024, 1024), 2)
+    got, fam = run(STRICT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert fam == "tcgen05"
+    for i in (0, 5, 7):
+        assert rel_frob(got[i], oracle.matmul(a[i], b[i])) <= STRICT_TOL
+
+
+# --------------------------------------------------------------- C5b GEMV --
+@pytest.mark.parametrize("m", [1, 4, 16])
+def test_c5b_gemv(oracle, m):
+    a = rng.randn((m, 4096), 1)
+    b = rng.randn((4096, 4096), 2)
+    ref = oracle.matmul(a, b)
+    got, fam = run(STRICT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert fam == "gemv" and rel_frob(got, ref) <= STRICT_TOL
+
+
+@pytest.mark.parametrize("m,k,n", [(3, 100, 64), (16, 8192, 260), (7, 1, 8), (1, 5000, 4)])
+def test_gemv_ragged(oracle, m, k, n):
+    a = rng.randn((m, k), 3)
+    b = rng.randn((k, n), 4)
+    bias = rng.randn((n,), 5)
+    ref = oracle.matmul(a, b, bias=bias, epilogue=oracle.EPI_BIAS_RELU)
+    got, fam = run(node(STRICT, epilogue=Epilogue.BIAS_RELU), DeviceView.from_host(a), DeviceView.from_host(b),
+                   DeviceView.from_host(bias))
+    assert fam == "gemv" and rel_frob(got, ref) <= STRICT_TOL
+
+
+# ------------------------------------------------------------ edge cases --
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (7, 9, 5), (127, 129, 33), (129, 255, 257), (255, 257, 129),
+                                   (128, 256, 32), (200, 300, 1000), (17, 520, 31)])
+def test_tcgen05_ragged_tiles(oracle, m, n, k):
+    a = rng.randn((m, k), m + 1)
+    b = rng.randn((k, n), n + 2)
+    ref = oracle.matmul(a, b)
+    for mode, tol in ((STRICT, STRICT_TOL), (TF32, TF32_TOL)):
+        got, fam = run(node(mode, family=KernelFamily.Tcgen05), padded(a), padded(b), out_dims=None)
+        assert fam == "tcgen05"
+        assert rel_frob(got, ref) <= tol, (m, n, k, mode.math_mode)
+    got, fam = run(EXACT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_output_pad_columns_untouched():
+    """A ragged output tile is clipped: padding beyond N keeps its bytes."""
+    a = DeviceView.from_host(rng.randn((130, 64), 1))
+    b = padded(rng.randn((64, 70), 2))
+    phys = DeviceView.from_host(np.full((130, 72), 7.0, np.float32))
+    out = phys.narrow(1, 0, 70)
+    with BoundGemm(STRICT, a, b, out) as g:
+        g.replay()
+        g.quiesce_or_abort()
+    host = phys.to_host()
+    assert np.all(host[:, 70:] == 7.0)
+
+
+def test_k_zero_and_empty(oracle):
+    a = DeviceView.contiguous(DeviceBuffer.allocate(4, 0), (5, 0))
+    b = DeviceView.contiguous(DeviceBuffer.allocate(4, 0), (0, 3))
+    bias = DeviceView.from_host(np.array([-1.0, 0.0, 2.0], np.float32))
+    out = DeviceView.from_host(np.full((5, 3), 9.0, np.float32))
+    with BoundGemm(node(STRICT, epilogue=Epilogue.BIAS_RELU), a, b, out, bias) as g:
+        g.replay()
+        g.quiesce_or_abort()
+    want = np.tile(np.array([0.0, 0.0, 2.0], np.float32), (5, 1))
+    got = out.to_host()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # empty output: a no-op bind and replay
+    e = DeviceView.contiguous(DeviceBuffer.allocate(4, 0), (0, 3))
+    with BoundGemm(STRICT, DeviceView.contiguous(DeviceBuffer.allocate(4, 0), (0, 4)),
+                   DeviceView.from_host(np.ones((4, 3), np.float32)), e) as g:
+        g.replay()
+        g.quiesce_or_abort()
+
+
+def test_nan_and_inf_propagate(oracle):
+    a = rng.randn((256, 128), 1)
+    b = rng.randn((128, 256), 2)
+    a[3, 7] = np.nan
+    a[10, 0] = np.inf
+    b[5, 9] = -np.inf
+    ref = oracle.matmul(a, b)
+    for mode in (STRICT, TF32):
+        got, _ = run(mode, DeviceView.from_host(a), DeviceView.from_host(b))
+        assert np.array_equal(np.isnan(got), np.isnan(ref)), mode.math_mode
+        fin = np.isfinite(ref)
+        assert np.array_equal(np.isinf(got), np.isinf(ref))
+        assert rel_frob(got[fin], ref[fin]) <= (STRICT_TOL if mode is STRICT else TF32_TOL)
+    got, _ = run(EXACT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    ok = ~np.isnan(ref)
+    assert np.array_equal(got[ok].view(np.uint32), ref[ok].view(np.uint32))
+
+
+def test_vector_operands(oracle):
+    a = rng.randn((300,), 1)
+    b = rng.randn((300, 40), 2)
+    ref = oracle.matmul(a.reshape(1, 300), b).reshape(40)
+    got, _ = run(STRICT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert got.shape == (40,) and rel_frob(got, ref) <= STRICT_TOL
+    bv = rng.randn((300,), 3)
+    ref = oracle.matmul(b.T.copy(), bv.reshape(300, 1)).reshape(40)
+    got, _ = run(EXACT, DeviceView.from_host(b.T.copy()), DeviceView.from_host(bv))
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_bind_rejects_host_memory_and_wrong_device():
+    host = np.zeros((64, 64), np.float32)
+    hv = DeviceView.contiguous(DeviceBuffer(host.ctypes.data, host.nbytes, 0), (64, 64))
+    dv = DeviceView.from_host(np.ones((64, 64), np.float32))
+    with pytest.raises(execution.UnsupportedDevice):
+        BoundGemm(STRICT, hv, dv, DeviceView.empty((64, 64)))
+    with pytest.raises(execution.UnsafeAliasing):
+        BoundGemm(STRICT, dv, dv, dv)
+
+
+def test_tf32_operands_are_truncated_by_the_tensor_core(oracle):
+    """Records how the tensor core reads f32 operands in kind::tf32: the TF32
+    result of raw inputs equals the TF32 result of inputs whose low 13
+    mantissa bits were cleared on the host (truncation), so the 3xTF32 split
+    hi = x & ~0x1FFF is the value the hardware multiplies."""
+    a = rng.randn((256, 256), 11)
+    b = rng.randn((256, 256), 12)
+    mask = np.uint32(0xFFFFE000)
+    at = (a.view(np.uint32) & mask).view(np.float32)
+    bt = (b.view(np.uint32) & mask).view(np.float32)
+    raw, _ = run(TF32, DeviceView.from_host(a), DeviceView.from_host(b))
+    trunc, _ = run(TF32, DeviceView.from_host(at), DeviceView.from_host(bt))
+    assert np.array_equal(raw.view(np.uint32), trunc.view(np.uint32))
