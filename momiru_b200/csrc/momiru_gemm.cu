@@ -360,10 +360,12 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D f32 tensor map {inner, outer, batch} with 128-byte swizzle.
+// 3-D f32 tensor map {inner, outer, batch} with a 128-byte swizzle: 16-byte
+// atoms for K-major operand tiles and the output, 32-byte atoms (the layout
+// tcgen05 kind::tf32 reads MN-major operands in) when `atom32` is set.
 int32_t encode_3d(CUtensorMap* tm, uint64_t base, uint64_t inner, uint64_t outer, uint64_t batch,
                   int64_t outer_stride_el, int64_t batch_stride_el, uint32_t box_inner, uint32_t box_outer,
-                  const char* name) {
+                  const char* name, bool atom32 = false) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(MMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   if (batch < 1) batch = 1;
@@ -378,7 +380,9 @@ int32_t encode_3d(CUtensorMap* tm, uint64_t base, uint64_t inner, uint64_t outer
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, reinterpret_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: cuTensorMapEncodeTiled failed (%d): dims {%llu,%llu,%llu}", name,
@@ -423,10 +427,22 @@ cudaError_t launch_tc(mmr_gemm_handle* h, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// Sets the shared-memory opt-in and checks the register split: setmaxnreg.inc
+// waits until the block's launch registers (threads x compiled count) can
+// cover the request, so a split larger than that would never proceed. Such a
+// build is refused here instead of launched.
 template <int MODE, bool AMN, bool BMN>
 cudaError_t prepare_tc(int smem) {
-  return cudaFuncSetAttribute(mmr::tc_gemm_kernel<MODE, AMN, BMN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              smem);
+  using Cfg = mmr::TcConfig<MODE>;
+  cudaError_t e = cudaFuncSetAttribute(mmr::tc_gemm_kernel<MODE, AMN, BMN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, mmr::tc_gemm_kernel<MODE, AMN, BMN>);
+  if (e != cudaSuccess) return e;
+  const long need = 2L * 128 * Cfg::kEpiRegs + long(Cfg::kThreads - 256) * Cfg::kOtherRegs;
+  if (long(fa.numRegs) * Cfg::kThreads < need) return cudaErrorInvalidConfiguration;
+  return cudaSuccess;
 }
 
 using TcLaunch = cudaError_t (*)(mmr_gemm_handle*, cudaStream_t);
@@ -643,10 +659,10 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     int32_t e;
     // A
     if (!t.a_mn) e = encode_3d(&h->tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, 32, mmr::TC_BM, "lhs");
-    else e = encode_3d(&h->tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, 32, "lhs");
+    else e = encode_3d(&h->tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, 32, "lhs", true);
     if (e) return cleanup(e);
     // B
-    if (t.b_mn) e = encode_3d(&h->tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, 32, "rhs");
+    if (t.b_mn) e = encode_3d(&h->tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, 32, "rhs", true);
     else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, 32, mmr::TC_BN, "rhs");
     if (e) return cleanup(e);
     // C
@@ -664,6 +680,12 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     if (tiles > INT32_MAX) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "too many output tiles"));
     q.tiles_total = int(tiles);
     q.k_blocks = int((p.k + mmr::TC_BK - 1) / mmr::TC_BK);
+    // StrictFp32 sums K in chunks of 256 (8 k-blocks) with round-to-nearest
+    // adds; one TF32 pass keeps a single chain per tile.
+    q.chunk_kb = h->mode ? 8 : q.k_blocks;
+    q.c = reinterpret_cast<float*>(p.c.base);
+    q.c_ld = p.c.s_r;
+    q.c_bs = t.c_sb;
     q.a_batched = t.a_batched;
     q.b_batched = t.b_batched;
     q.epilogue = p.epilogue;
@@ -674,6 +696,8 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     h->grid = dim3(unsigned(std::min<int64_t>(tiles, sms)));
     h->block = dim3(h->mode ? mmr::TcConfig<1>::kThreads : mmr::TcConfig<0>::kThreads);
     cudaError_t ce = tc_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
+    if (ce == cudaErrorInvalidConfiguration)
+      return cleanup(fail(MMR_ERR_CUDA, "tcgen05 kernel was compiled with too few registers for its warp split"));
     if (ce != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce)));
     h->info.a_mn_major = t.a_mn;
     h->info.b_mn_major = t.b_mn;

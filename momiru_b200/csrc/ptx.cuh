@@ -171,7 +171,8 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): start
 // address, leading/stride byte offsets (>>4), version 1 at bit 46, layout
-// type at bits 61..63 (2 = 128-byte swizzle).
+// type at bits 61..63 (2 = 128-byte swizzle of 16-byte atoms, 1 = 128-byte
+// swizzle of 32-byte atoms, the only MN-major layout for tf32 operands).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
                                               uint32_t layout) {
   uint64_t d = 0;

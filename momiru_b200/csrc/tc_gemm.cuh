@@ -7,16 +7,22 @@
 // (src/momiru/tensor_light/execution/cpu.rs:2989-3098) for a GPU node.
 //
 // Roles (one CTA per SM, persistent over output tiles of BM x BN):
-//   warps 0-3  epilogue: TMEM -> registers (tcgen05.ld) -> +bias, ReLU ->
-//              swizzled shared staging -> TMA store (coalesced, clipped)
-//   warp 4     producer: TMA loads of A/B k-blocks into an S-stage ring
-//   warp 5     MMA issuer: tcgen05.mma kind::tf32 into a double-buffered
-//              TMEM accumulator (2 x 256 columns)
-//   warps 6-9  (3xTF32 only) split: each staged f32 operand x becomes
-//              hi = x with the low 13 mantissa bits cleared (exact in TF32)
-//              and lo = x - hi (exact in f32); the MMA issuer then runs
-//              hi*hi + hi*lo + lo*hi per k-step (the error-corrected TF32
-//              method of Ootomo & Yokota, 2022).
+//   warps 0-7   epilogue (two warpgroups; warp w reads TMEM lane quarter w%4
+//               and column half w/4): sums K-chunk partials out of TMEM into
+//               f32 registers with round-to-nearest adds, then +bias, ReLU,
+//               swizzled shared staging and a TMA store (clipped at the
+//               tensor edge; a ragged right edge uses guarded plain stores)
+//   warp 8      producer: TMA loads of A/B k-blocks into an S-stage ring
+//   warp 9      MMA issuer: tcgen05.mma kind::tf32 into two TMEM partial
+//               accumulators of 256 columns, alternating per K-chunk
+//   warps 10-15 (3xTF32 only) split: each staged f32 operand x becomes
+//               hi = x with the low 13 mantissa bits cleared (exact in TF32)
+//               and lo = x - hi (exact in f32); the MMA issuer then runs
+//               lo*hi + hi*lo + hi*hi per k-step (the error-corrected TF32
+//               method of Ootomo & Yokota, 2022).
+// K is accumulated in chunks of `chunk_kb` k-blocks: the tensor core's f32
+// accumulation is not round-to-nearest, so a single 8192-long chain drifts by
+// ~6e-5 relative; short chains summed with RN adds stay near 2e-6.
 // Every wait is bounded; on expiry the kernel records an error word, drains
 // its in-flight copies and MMAs (bounded), frees TMEM and returns.
 #pragma once
@@ -31,8 +37,11 @@ constexpr int TC_A_BYTES = TC_BM * TC_BK * 4;   // 16 KiB
 constexpr int TC_B_BYTES = TC_BN * TC_BK * 4;   // 32 KiB
 constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_CSTAGE_BYTES = 32 * 32 * 4;    // one 32x32 f32 store box
-constexpr int TC_EPI_WARPS = 4;
-constexpr int TC_SPLIT_WARPS = 4;
+constexpr int TC_EPI_WARPS = 8;
+constexpr int TC_PRODUCER_WARP = 8;
+constexpr int TC_MMA_WARP = 9;
+constexpr int TC_SPLIT_WARP0 = 10;
+constexpr int TC_SPLIT_WARPS = 6;
 constexpr int TC_GROUP_M = 16;                  // tile raster: M-tiles per group
 
 enum : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU = 3 };
@@ -40,12 +49,22 @@ enum : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU = 3 };
 template <int MODE>
 struct TcConfig {
   static constexpr int kStages = MODE ? 2 : 4;
-  static constexpr int kThreads = 32 * (6 + (MODE ? TC_SPLIT_WARPS : 0));
+  static constexpr int kWarps = MODE ? 16 : 12;
+  static constexpr int kThreads = 32 * kWarps;
+  // Register split by warpgroup (setmaxnreg): the two epilogue warpgroups
+  // hold a 128-float running sum per thread; the others need few registers.
+  // Launch budget = kThreads * kLaunchRegs; the sum of the split must fit it
+  // (checked on the host against the compiled register count before launch).
+  static constexpr int kLaunchRegs = MODE ? 128 : 168;
+  static constexpr int kEpiRegs = MODE ? 176 : 200;
+  static constexpr int kOtherRegs = MODE ? 80 : 96;
   static constexpr int kOperandBytes = kStages * TC_STAGE_BYTES * (MODE ? 2 : 1);
-  static constexpr int kCstageBytes = TC_EPI_WARPS * 2 * TC_CSTAGE_BYTES;
+  static constexpr int kCstageBytes = TC_EPI_WARPS * TC_CSTAGE_BYTES;
   static constexpr int kBarrierBytes = 256;
   // +1024 so the kernel can round its dynamic base up to 1024 bytes.
   static constexpr int kSmemBytes = kOperandBytes + kCstageBytes + kBarrierBytes + 1024;
+  static_assert(2 * 128 * kEpiRegs + (kWarps - 8) * 32 * kOtherRegs <= kThreads * kLaunchRegs,
+                "register split exceeds the launch budget");
 };
 
 struct TcParams {
@@ -54,9 +73,12 @@ struct TcParams {
   int tiles_m, tiles_n;
   int tiles_total;
   int k_blocks;
+  int chunk_kb;              // k-blocks per TMEM accumulation chunk
   int a_batched, b_batched;  // 0: operand broadcast over the batch
   int epilogue;
   const float* bias;         // [n] when the epilogue adds a bias
+  float* c;                  // output base (for the ragged right edge)
+  long long c_ld, c_bs;      // output row / batch strides (elements)
   int* err;                  // device error word
   unsigned long long timeout_ns;
 };
@@ -74,6 +96,15 @@ __device__ __forceinline__ void tc_tile_coords(const TcParams& p, int t, int& mt
   nt = q / gsize;
 }
 
+template <int N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(N));
+}
+
 template <int MODE, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -84,13 +115,13 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ops = smem;                                     // [S][A|B]
   uint8_t* lo_ops = smem + S * TC_STAGE_BYTES;             // [S][Alo|Blo] (3xTF32)
-  uint8_t* cstage = smem + Cfg::kOperandBytes;             // [4 warps][2][32x32]
+  uint8_t* cstage = smem + Cfg::kOperandBytes;             // [8 warps][32x32]
   uint64_t* bars = reinterpret_cast<uint64_t*>(cstage + Cfg::kCstageBytes);
   uint64_t* full = bars;             // [S] TMA -> split/MMA
   uint64_t* split_done = bars + S;   // [S] split -> MMA (3xTF32)
   uint64_t* empty = bars + 2 * S;    // [S] MMA -> TMA
-  uint64_t* acc_full = bars + 3 * S; // [2] MMA -> epilogue
-  uint64_t* acc_empty = acc_full + 2;// [2] epilogue -> MMA
+  uint64_t* acc_full = bars + 3 * S; // [2] MMA -> epilogue (a K-chunk is done)
+  uint64_t* acc_empty = acc_full + 2;// [2] epilogue -> MMA (partial consumed)
   uint64_t* drain = acc_full + 4;    // [1] teardown of the MMA pipe
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -111,12 +142,12 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
     mbar_init(drain, 1);
     fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == TC_PRODUCER_WARP && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
   }
-  if (warp == 5) {
+  if (warp == TC_MMA_WARP) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -124,188 +155,224 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const int n_chunks = (p.k_blocks + p.chunk_kb - 1) / p.chunk_kb;
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued_parity[S];
-      for (int s = 0; s < S; ++s) issued_parity[s] = -1;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
-        int mt, nt, bt;
-        tc_tile_coords(p, t, mt, nt, bt);
-        const int m0 = mt * TC_BM, n0 = nt * TC_BN;
-        const int ba = p.a_batched ? bt : 0, bb = p.b_batched ? bt : 0;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, ctl, kDevTimeoutEmpty)) { ok = false; break; }
-          uint8_t* sa = ops + stage * TC_STAGE_BYTES;
-          uint8_t* sb = sa + TC_A_BYTES;
-          const int k0 = kb * TC_BK;
-          mbar_arrive_expect_tx(&full[stage], TC_STAGE_BYTES);
-          if (A_MN) {
-#pragma unroll
-            for (int i = 0; i < TC_BM / 32; ++i) tma_load_3d(sa + i * 4096, &tmA, &full[stage], m0 + 32 * i, k0, ba);
-          } else {
-            tma_load_3d(sa, &tmA, &full[stage], k0, m0, ba);
-          }
-          if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < TC_BN / 32; ++j) tma_load_3d(sb + j * 4096, &tmB, &full[stage], n0 + 32 * j, k0, bb);
-          } else {
-            tma_load_3d(sb, &tmB, &full[stage], k0, n0, bb);
-          }
-          issued_parity[stage] = static_cast<int>(phase);
-          if (++stage == S) { stage = 0; phase ^= 1u; }
-        }
-      }
-      // Drain: every load this thread issued must have landed before the CTA
-      // may exit (immediate on the normal path).
-      WaitCtl drain_ctl{p.err, p.timeout_ns};
-      for (int s = 0; s < S; ++s) {
-        if (issued_parity[s] >= 0) {
-          uint32_t a = smem_u32(&full[s]);
-          uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(a, static_cast<uint32_t>(issued_parity[s]))) {
-            if (globaltimer_ns() - t0 > drain_ctl.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
-          }
-        }
-      }
-    }
-  } else if (warp == 5) {
-    // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(TC_BM, TC_BN, A_MN, B_MN);
-      // Descriptor geometry (bytes). K-major 128B-swizzle: rows of 128 B,
-      // 8-row groups 1024 B apart, +32 B per 8-wide k-step. MN-major
-      // 128B-swizzle: 32-element MN atoms 4096 B apart (LBO), 8-row K groups
-      // 1024 B apart (SBO), +1024 B per k-step.
-      constexpr uint32_t a_lbo = A_MN ? 4096u : 16u, a_sbo = 1024u, a_kstep = A_MN ? 1024u : 32u;
-      constexpr uint32_t b_lbo = B_MN ? 4096u : 16u, b_sbo = 1024u, b_kstep = B_MN ? 1024u : 32u;
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
-      bool ok = true;
-      bool issued_any = false;
-      for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
-        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
-          uint64_t* ready = MODE ? &split_done[stage] : &full[stage];
-          if (!mbar_wait(ready, phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t sa = smem_u32(ops + stage * TC_STAGE_BYTES);
-          const uint32_t sb = sa + TC_A_BYTES;
-          const uint32_t sa_lo = smem_u32(lo_ops + stage * TC_STAGE_BYTES);
-          const uint32_t sb_lo = sa_lo + TC_A_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < TC_BK / 8; ++kk) {
-            const uint64_t ad = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, 2);
-            const uint64_t bd = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, 2);
-            if (MODE) {
-              const uint64_t ad_lo = smem_desc(sa_lo + kk * a_kstep, a_lbo, a_sbo, 2);
-              const uint64_t bd_lo = smem_desc(sb_lo + kk * b_kstep, b_lbo, b_sbo, 2);
-              // Small cross terms first, then hi*hi.
-              umma_tf32(d_tmem, ad_lo, bd, idesc, (kb | kk) != 0);
-              umma_tf32(d_tmem, ad, bd_lo, idesc, 1u);
-              umma_tf32(d_tmem, ad, bd, idesc, 1u);
-            } else {
-              umma_tf32(d_tmem, ad, bd, idesc, (kb | kk) != 0);
-            }
-          }
-          issued_any = true;
-          umma_commit(&empty[stage]);
-          if (++stage == S) { stage = 0; phase ^= 1u; }
-        }
-        if (!ok) break;
-        umma_commit(&acc_full[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-      }
-      if (issued_any) {
-        // Every MMA must have finished before TMEM is freed.
-        umma_commit(drain);
-        uint32_t a = smem_u32(drain);
-        uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(a, 0u)) {
-          if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
-        }
-      }
-    }
-  } else if (warp < TC_EPI_WARPS) {
+  if (warp < TC_EPI_WARPS) {
+    reg_alloc<Cfg::kEpiRegs>();
     // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3, half = warp >> 2;
     int acc = 0;
     uint32_t acc_phase = 0;
-    uint8_t* my_stage = cstage + warp * 2 * TC_CSTAGE_BYTES;
-    int chunk_count = 0;
+    uint8_t* buf = cstage + warp * TC_CSTAGE_BYTES;
     const bool add_bias = (p.epilogue == EPI_BIAS || p.epilogue == EPI_BIAS_RELU);
     const bool relu = (p.epilogue == EPI_BIAS_RELU || p.epilogue == EPI_RELU);
-    for (int t = blockIdx.x; t < p.tiles_total; t += gridDim.x) {
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
       int mt, nt, bt;
       tc_tile_coords(p, t, mt, nt, bt);
       const int m0 = mt * TC_BM, n0 = nt * TC_BN;
-      if (!mbar_wait(&acc_full[acc], acc_phase, ctl, kDevTimeoutAcc)) break;
-      tc_fence_after();
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc * TC_BN);
-#pragma unroll 1
-      for (int c = 0; c < TC_BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        if (c == TC_BN / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(&acc_empty[acc]);
+      float sum[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) sum[i] = 0.0f;
+      for (int c = 0; c < n_chunks; ++c) {
+        if (!mbar_wait(&acc_full[acc], acc_phase, ctl, kDevTimeoutAcc)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                            static_cast<uint32_t>(acc * TC_BN + half * 128);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tb + j * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sum[j * 32 + i] = __fadd_rn(sum[j * 32 + i], __uint_as_float(r[i]));
         }
-        const int col0 = n0 + c * 32;
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok) break;
+      const int row0 = m0 + quarter * 32;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col0 = n0 + half * 128 + j * 32;
         float bias_lane = 0.0f;
         if (add_bias && col0 + lane < p.n) bias_lane = __ldg(p.bias + col0 + lane);
-        float v[32];
+        float* v = sum + j * 32;  // epilogue applied in place
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(r[i]);
+          float x = v[i];
           if (add_bias) x = __fadd_rn(x, __shfl_sync(0xffffffffu, bias_lane, i));
           if (relu) x = (x != x) ? x : (x > 0.0f ? x : 0.0f);
           v[i] = x;
         }
-        uint8_t* buf = my_stage + (chunk_count & 1) * TC_CSTAGE_BYTES;
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        // 128B-swizzled row `lane`: 16-byte chunk j lives at j ^ (lane & 7).
+        if (row0 >= p.m || col0 >= p.n) continue;  // wholly outside C (warp-uniform)
+        if ((p.n & 3) && col0 + 32 > p.n) {
+          // Ragged right edge: TMA writes whole 16-byte chunks, so store the
+          // valid columns one by one instead.
+          const int row = row0 + lane;
+          if (row < p.m) {
+            float* dst = p.c + (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float4 q = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-          *reinterpret_cast<float4*>(buf + lane * 128 + ((j ^ (lane & 7)) << 4)) = q;
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.n) dst[i] = v[i];
+          }
+          continue;
+        }
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+        // 128B-swizzled row `lane`: 16-byte chunk q lives at q ^ (lane & 7).
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 w4 = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) = w4;
         }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          // Boxes wholly outside C are skipped; partial ones are clipped by TMA.
-          if (m0 + warp * 32 < p.m && col0 < p.n) tma_store_3d(&tmC, buf, col0, m0 + warp * 32, bt);
+          tma_store_3d(&tmC, buf, col0, row0, bt);
           bulk_commit_group();
         }
-        ++chunk_count;
       }
-      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
     if (lane == 0) bulk_wait_group_all();
     __syncwarp();
-  } else if (MODE) {
-    // --------------------------------------------------- 3xTF32 split warps
-    const int tid = threadIdx.x - 6 * 32;
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        if (!mbar_wait(&full[stage], phase, ctl, kDevTimeoutFull)) { ok = false; break; }
-        uint4* x = reinterpret_cast<uint4*>(ops + stage * TC_STAGE_BYTES);
-        uint4* lo = reinterpret_cast<uint4*>(lo_ops + stage * TC_STAGE_BYTES);
+  } else {
+    reg_dealloc<Cfg::kOtherRegs>();
+    if (warp == TC_PRODUCER_WARP) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued_parity[S];
+        for (int s = 0; s < S; ++s) issued_parity[s] = -1;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
+          int mt, nt, bt;
+          tc_tile_coords(p, t, mt, nt, bt);
+          const int m0 = mt * TC_BM, n0 = nt * TC_BN;
+          const int ba = p.a_batched ? bt : 0, bb = p.b_batched ? bt : 0;
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!mbar_wait(&empty[stage], phase ^ 1u, ctl, kDevTimeoutEmpty)) { ok = false; break; }
+            uint8_t* sa = ops + stage * TC_STAGE_BYTES;
+            uint8_t* sb = sa + TC_A_BYTES;
+            const int k0 = kb * TC_BK;
+            mbar_arrive_expect_tx(&full[stage], TC_STAGE_BYTES);
+            if (A_MN) {
+#pragma unroll
+              for (int i = 0; i < TC_BM / 32; ++i)
+                tma_load_3d(sa + i * 4096, &tmA, &full[stage], m0 + 32 * i, k0, ba);
+            } else {
+              tma_load_3d(sa, &tmA, &full[stage], k0, m0, ba);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < TC_BN / 32; ++j)
+                tma_load_3d(sb + j * 4096, &tmB, &full[stage], n0 + 32 * j, k0, bb);
+            } else {
+              tma_load_3d(sb, &tmB, &full[stage], k0, n0, bb);
+            }
+            issued_parity[stage] = static_cast<int>(phase);
+            if (++stage == S) { stage = 0; phase ^= 1u; }
+          }
+        }
+        // Drain: every load this thread issued must have landed before the
+        // CTA may exit (immediate on the normal path).
+        for (int s = 0; s < S; ++s) {
+          if (issued_parity[s] >= 0) {
+            const uint32_t a = smem_u32(&full[s]);
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(a, static_cast<uint32_t>(issued_parity[s]))) {
+              if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
+            }
+          }
+        }
+      }
+    } else if (warp == TC_MMA_WARP) {
+      // -------------------------------------------------------- MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t idesc = idesc_tf32(TC_BM, TC_BN, A_MN, B_MN);
+        // Descriptor geometry (bytes).
+        //  K-major, 128-byte swizzle (layout 2, 16-byte atoms): rows of 128 B,
+        //  8-row groups 1024 B apart (SBO), +32 B per 8-wide k-step.
+        //  MN-major tf32 must use the 128-byte swizzle with 32-byte atoms
+        //  (layout 1, TMA SWIZZLE_128B_ATOM_32B): 32-element MN atoms 4096 B
+        //  apart (LBO), 4-row K groups 512 B apart (SBO), +1024 B per k-step.
+        constexpr uint32_t a_layout = A_MN ? 1u : 2u, b_layout = B_MN ? 1u : 2u;
+        constexpr uint32_t a_lbo = A_MN ? 4096u : 16u, a_sbo = A_MN ? 512u : 1024u, a_kstep = A_MN ? 1024u : 32u;
+        constexpr uint32_t b_lbo = B_MN ? 4096u : 16u, b_sbo = B_MN ? 512u : 1024u, b_kstep = B_MN ? 1024u : 32u;
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        bool issued_any = false;
+        for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
+          uint32_t d_tmem = 0;
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            const int kc = kb % p.chunk_kb;
+            if (kc == 0) {
+              if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
+              tc_fence_after();
+              d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
+            }
+            uint64_t* ready = MODE ? &split_done[stage] : &full[stage];
+            if (!mbar_wait(ready, phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(ops + stage * TC_STAGE_BYTES);
+            const uint32_t sb = sa + TC_A_BYTES;
+            const uint32_t sa_lo = smem_u32(lo_ops + stage * TC_STAGE_BYTES);
+            const uint32_t sb_lo = sa_lo + TC_A_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 8; ++kk) {
+              const uint64_t ad = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_layout);
+              const uint64_t bd = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_layout);
+              const uint32_t accumulate = (kc | kk) != 0;
+              if (MODE) {
+                const uint64_t ad_lo = smem_desc(sa_lo + kk * a_kstep, a_lbo, a_sbo, a_layout);
+                const uint64_t bd_lo = smem_desc(sb_lo + kk * b_kstep, b_lbo, b_sbo, b_layout);
+                // Small cross terms first, then hi*hi.
+                umma_tf32(d_tmem, ad_lo, bd, idesc, accumulate);
+                umma_tf32(d_tmem, ad, bd_lo, idesc, 1u);
+                umma_tf32(d_tmem, ad, bd, idesc, 1u);
+              } else {
+                umma_tf32(d_tmem, ad, bd, idesc, accumulate);
+              }
+            }
+            issued_any = true;
+            umma_commit(&empty[stage]);
+            if (++stage == S) { stage = 0; phase ^= 1u; }
+            if (kc == p.chunk_kb - 1 || kb == p.k_blocks - 1) {
+              umma_commit(&acc_full[acc]);
+              if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+          }
+        }
+        if (issued_any) {
+          // Every MMA must have finished before TMEM is freed.
+          umma_commit(drain);
+          const uint32_t a = smem_u32(drain);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(a, 0u)) {
+            if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
+          }
+        }
+      }
+    } else if (MODE && warp >= TC_SPLIT_WARP0 && warp < TC_SPLIT_WARP0 + TC_SPLIT_WARPS) {
+      // ------------------------------------------------- 3xTF32 split warps
+      const int tid = threadIdx.x - TC_SPLIT_WARP0 * 32;
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, ctl, kDevTimeoutFull)) { ok = false; break; }
+          uint4* x = reinterpret_cast<uint4*>(ops + stage * TC_STAGE_BYTES);
+          uint4* lo = reinterpret_cast<uint4*>(lo_ops + stage * TC_STAGE_BYTES);
 #pragma unroll 4
-        for (int i = tid; i < TC_STAGE_BYTES / 16; i += TC_SPLIT_WARPS * 32) {
-          uint4 v = x[i];
-          uint4 h, l;
+          for (int i = tid; i < TC_STAGE_BYTES / 16; i += TC_SPLIT_WARPS * 32) {
+            uint4 v = x[i];
+            uint4 h, l;
 #define MMR_SPLIT1(F)                                                                     \
   {                                                                                       \
     const uint32_t u = v.F;                                                               \
@@ -317,21 +384,22 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
       l.F = __float_as_uint(__fsub_rn(__uint_as_float(u), __uint_as_float(h.F)));        \
     }                                                                                     \
   }
-          MMR_SPLIT1(x) MMR_SPLIT1(y) MMR_SPLIT1(z) MMR_SPLIT1(w)
+            MMR_SPLIT1(x) MMR_SPLIT1(y) MMR_SPLIT1(z) MMR_SPLIT1(w)
 #undef MMR_SPLIT1
-          x[i] = h;
-          lo[i] = l;
+            x[i] = h;
+            lo[i] = l;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&split_done[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1u; }
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&split_done[stage]);
-        if (++stage == S) { stage = 0; phase ^= 1u; }
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == TC_MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
   }

@@ -189,7 +189,7 @@ def test_c3_full_size_row_sampled(oracle):
     plain, _ = run(STRICT, da, db)
     lhs = plain.astype(np.float64).sum(axis=0)
     rhs = a.astype(np.float64).sum(axis=0) @ b.astype(np.float64)
-    assert rel_frob(lhs, rhs) <= 1e-6
+    assert rel_frob(lhs, rhs) <= STRICT_TOL
 
 
 # ----------------------------------------------------- C4 strided views --
