@@ -414,6 +414,8 @@ struct mmr_gemm_handle {
   int smem = 0;
   int* d_err = nullptr;
   int* h_err = nullptr;  // pinned host copy of the error word
+  unsigned int* d_nf = nullptr;  // 3xTF32 non-finite bookkeeping
+  int sms = 148;
   cudaEvent_t done = nullptr, err_ev = nullptr;
   bool ran = false;
   uint64_t wait_timeout_ns = 2000000000ull;
@@ -502,6 +504,24 @@ cudaError_t prepare_gemv(int mt, int smem) {
     case 8: return prepare_gemv_mt<8>(smem);
     default: return prepare_gemv_mt<16>(smem);
   }
+}
+
+void fill_simt_params(const Plan& p, mmr::SimtParams* sp) {
+  mmr::SimtParams& s = *sp;
+  s.m = int(p.m);
+  s.n = int(p.n);
+  s.k = int(p.k);
+  s.batch0 = int(p.batch0);
+  s.batch1 = int(p.batch1);
+  s.a = reinterpret_cast<const float*>(p.a.base);
+  s.a_b0 = p.a.s_b0; s.a_b1 = p.a.s_b1; s.a_m = p.a.s_r; s.a_k = p.a.s_c;
+  s.b = reinterpret_cast<const float*>(p.b.base);
+  s.b_b0 = p.b.s_b0; s.b_b1 = p.b.s_b1; s.b_k = p.b.s_r; s.b_n = p.b.s_c;
+  s.c = reinterpret_cast<float*>(p.c.base);
+  s.c_b0 = p.c.s_b0; s.c_b1 = p.c.s_b1; s.c_m = p.c.s_r; s.c_n = p.c.s_c;
+  s.bias = reinterpret_cast<const float*>(p.bias);
+  s.bias_n = p.bias_s;
+  s.epilogue = p.epilogue;
 }
 
 void fill_info_common(const Plan& p, mmr_gemm_info* info) {
@@ -692,6 +712,16 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     q.bias = reinterpret_cast<const float*>(p.bias);
     q.err = h->d_err;
     q.timeout_ns = h->wait_timeout_ns;
+    q.nf = nullptr;
+    if (h->mode == 1) {
+      const size_t words = 2 + 2 * size_t(tiles);
+      if (cudaMalloc(&h->d_nf, words * sizeof(unsigned int)) != cudaSuccess ||
+          cudaMemset(h->d_nf, 0, words * sizeof(unsigned int)) != cudaSuccess)
+        return cleanup(fail(MMR_ERR_CUDA, "allocating the non-finite bookkeeping failed"));
+      q.nf = h->d_nf;
+      fill_simt_params(p, &h->sp);
+    }
+    h->sms = sms;
     h->smem = h->mode ? mmr::TcConfig<1>::kSmemBytes : mmr::TcConfig<0>::kSmemBytes;
     h->grid = dim3(unsigned(std::min<int64_t>(tiles, sms)));
     h->block = dim3(h->mode ? mmr::TcConfig<1>::kThreads : mmr::TcConfig<0>::kThreads);
@@ -736,21 +766,7 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
   if (fam == MMR_FAMILY_SIMT) {
     h->family = fam;
     h->info.family = fam;
-    mmr::SimtParams& s = h->sp;
-    s.m = int(p.m);
-    s.n = int(p.n);
-    s.k = int(p.k);
-    s.batch0 = int(p.batch0);
-    s.batch1 = int(p.batch1);
-    s.a = reinterpret_cast<const float*>(p.a.base);
-    s.a_b0 = p.a.s_b0; s.a_b1 = p.a.s_b1; s.a_m = p.a.s_r; s.a_k = p.a.s_c;
-    s.b = reinterpret_cast<const float*>(p.b.base);
-    s.b_b0 = p.b.s_b0; s.b_b1 = p.b.s_b1; s.b_k = p.b.s_r; s.b_n = p.b.s_c;
-    s.c = reinterpret_cast<float*>(p.c.base);
-    s.c_b0 = p.c.s_b0; s.c_b1 = p.c.s_b1; s.c_m = p.c.s_r; s.c_n = p.c.s_c;
-    s.bias = reinterpret_cast<const float*>(p.bias);
-    s.bias_n = p.bias_s;
-    s.epilogue = p.epilogue;
+    fill_simt_params(p, &h->sp);
     if (batch > 65535) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "batch too large for the SIMT family"));
     h->grid = dim3(unsigned((p.n + mmr::SIMT_BN - 1) / mmr::SIMT_BN), unsigned((p.m + mmr::SIMT_BM - 1) / mmr::SIMT_BM),
                    unsigned(batch));
@@ -774,7 +790,13 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
   cudaError_t e = cudaSuccess;
   if (!h->plan.empty) {
     switch (h->family) {
-      case MMR_FAMILY_TCGEN05: e = tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s); break;
+      case MMR_FAMILY_TCGEN05:
+        e = tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s);
+        if (e == cudaSuccess && h->mode == 1) {
+          mmr::tc_nonfinite_fixup_kernel<<<h->sms, 256, 0, s>>>(h->sp, h->tcp);
+          e = cudaGetLastError();
+        }
+        break;
       case MMR_FAMILY_GEMV: e = launch_gemv(h, s); break;
       case MMR_FAMILY_SIMT:
         mmr::simt_gemm_exact_kernel<<<h->grid, h->block, 0, s>>>(h->sp);
@@ -838,6 +860,7 @@ int32_t mmr_gemm_destroy(mmr_gemm_handle* h) {
     if (h->done) cudaEventDestroy(h->done);
     if (h->err_ev) cudaEventDestroy(h->err_ev);
     if (h->d_err) cudaFree(h->d_err);
+    if (h->d_nf) cudaFree(h->d_nf);
     if (h->h_err) cudaFreeHost(h->h_err);
   }
   delete h;

@@ -25,12 +25,11 @@ struct SimtParams {
 
 constexpr int SIMT_BM = 64, SIMT_BN = 64, SIMT_BK = 16;
 
-__global__ void __launch_bounds__(256) simt_gemm_exact_kernel(const SimtParams p) {
-  __shared__ float As[SIMT_BK][SIMT_BM + 4];
-  __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
+// One 64x64 output block (rows m0.., cols n0.. of flat batch entry bz) in the
+// reference's exact order, written through the epilogue. 256 threads.
+__device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, int n0, int bz,
+                                                 float (*As)[SIMT_BM + 4], float (*Bs)[SIMT_BN + 4]) {
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int n0 = blockIdx.x * SIMT_BN, m0 = blockIdx.y * SIMT_BM;
-  const int bz = blockIdx.z;
   const int b0 = bz / p.batch1, b1 = bz - (bz / p.batch1) * p.batch1;
   const float* A = p.a + b0 * p.a_b0 + b1 * p.a_b1;
   const float* B = p.b + b0 * p.b_b0 + b1 * p.b_b1;
@@ -85,6 +84,12 @@ __global__ void __launch_bounds__(256) simt_gemm_exact_kernel(const SimtParams p
       C[gm * p.c_m + gn * p.c_n] = x;
     }
   }
+}
+
+__global__ void __launch_bounds__(256) simt_gemm_exact_kernel(const SimtParams p) {
+  __shared__ float As[SIMT_BK][SIMT_BM + 4];
+  __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
+  simt_block_exact(p, blockIdx.y * SIMT_BM, blockIdx.x * SIMT_BN, blockIdx.z, As, Bs);
 }
 
 }  // namespace mmr

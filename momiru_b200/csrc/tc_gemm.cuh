@@ -25,8 +25,14 @@
 // ~6e-5 relative; short chains summed with RN adds stay near 2e-6.
 // Every wait is bounded; on expiry the kernel records an error word, drains
 // its in-flight copies and MMAs (bounded), frees TMEM and returns.
+// Inputs holding inf or NaN: in 3xTF32 the cross term hi(inf) * lo(b) is
+// inf * 0 = NaN whenever b is exactly representable in TF32, which the
+// reference order never produces. The split warps flag such tiles (a rare
+// path: one atomic per affected stage) and tc_nonfinite_fixup_kernel then
+// recomputes every output of a flagged tile in the reference's exact order.
 #pragma once
 #include "ptx.cuh"
+#include "simt_gemm.cuh"
 
 namespace mmr {
 
@@ -81,6 +87,9 @@ struct TcParams {
   long long c_ld, c_bs;      // output row / batch strides (elements)
   int* err;                  // device error word
   unsigned long long timeout_ns;
+  // Non-finite bookkeeping (3xTF32): [0] count, [1] blocks done,
+  // [2, 2+tiles) per-tile flags, [2+tiles, 2+2*tiles) flagged tile list.
+  unsigned int* nf;
 };
 
 __device__ __forceinline__ void tc_tile_coords(const TcParams& p, int t, int& mt, int& nt, int& bt) {
@@ -369,6 +378,7 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
           if (!mbar_wait(&full[stage], phase, ctl, kDevTimeoutFull)) { ok = false; break; }
           uint4* x = reinterpret_cast<uint4*>(ops + stage * TC_STAGE_BYTES);
           uint4* lo = reinterpret_cast<uint4*>(lo_ops + stage * TC_STAGE_BYTES);
+          bool nonfinite = false;
 #pragma unroll 4
           for (int i = tid; i < TC_STAGE_BYTES / 16; i += TC_SPLIT_WARPS * 32) {
             uint4 v = x[i];
@@ -379,6 +389,7 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
     if ((u & 0x7F800000u) == 0x7F800000u) {                                               \
       h.F = (u & 0x007FFFFFu) ? 0x7FC00000u : u;                                          \
       l.F = 0u;                                                                           \
+      nonfinite = true;                                                                   \
     } else {                                                                              \
       h.F = u & 0xFFFFE000u;                                                              \
       l.F = __float_as_uint(__fsub_rn(__uint_as_float(u), __uint_as_float(h.F)));        \
@@ -391,6 +402,9 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
           }
           fence_proxy_async_smem();
           mbar_arrive(&split_done[stage]);
+          if (__any_sync(0xffffffffu, nonfinite) && lane == 0 && p.nf != nullptr) {
+            if (atomicOr(&p.nf[2 + t], 1u) == 0u) p.nf[2 + p.tiles_total + atomicAdd(&p.nf[0], 1u)] = t;
+          }
           if (++stage == S) { stage = 0; phase ^= 1u; }
         }
       }
@@ -402,6 +416,40 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
   if (warp == TC_MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// Recomputes, in the reference's exact order, every output of the tiles the
+// split warps flagged, then clears the bookkeeping for the next run (the last
+// block to finish does it). With nothing flagged every block returns at once.
+__global__ void __launch_bounds__(256) tc_nonfinite_fixup_kernel(const SimtParams sp, const TcParams p) {
+  __shared__ float As[SIMT_BK][SIMT_BM + 4];
+  __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
+  __shared__ bool last;
+  const unsigned int count = *reinterpret_cast<volatile unsigned int*>(&p.nf[0]);
+  if (count == 0) return;
+  constexpr int kSub = (TC_BM / SIMT_BM) * (TC_BN / SIMT_BN);
+  for (unsigned int w = blockIdx.x; w < count * kSub; w += gridDim.x) {
+    const int t = static_cast<int>(p.nf[2 + p.tiles_total + w / kSub]);
+    const int sub = static_cast<int>(w % kSub);
+    int mt, nt, bt;
+    tc_tile_coords(p, t, mt, nt, bt);
+    const int m0 = mt * TC_BM + (sub / (TC_BN / SIMT_BN)) * SIMT_BM;
+    const int n0 = nt * TC_BN + (sub % (TC_BN / SIMT_BN)) * SIMT_BN;
+    simt_block_exact(sp, m0, n0, bt, As, Bs);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = (atomicAdd(&p.nf[1], 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (last) {
+    __threadfence();
+    for (unsigned int i = threadIdx.x; i < count; i += blockDim.x) p.nf[2 + p.nf[2 + p.tiles_total + i]] = 0u;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      p.nf[0] = 0u;
+      p.nf[1] = 0u;
+    }
   }
 }
 

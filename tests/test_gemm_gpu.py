@@ -324,6 +324,33 @@ def test_nan_and_inf_propagate(oracle):
     assert np.array_equal(got[ok].view(np.uint32), ref[ok].view(np.uint32))
 
 
+def test_nonfinite_bookkeeping_resets_between_runs(oracle):
+    """A replay with inf/NaN inputs, then finite inputs in the same buffers:
+    the second result is the ordinary 3xTF32 one, within tolerance."""
+    a = rng.randn((384, 256), 1)
+    b = rng.randn((256, 512), 2)
+    bad = a.copy()
+    bad[100, 3] = np.inf
+    bad[300, 9] = np.nan
+    da, db = DeviceView.from_host(bad), DeviceView.from_host(b)
+    out = DeviceView.empty((384, 512))
+    with BoundGemm(STRICT, da, db, out) as g:
+        g.replay()
+        g.quiesce_or_abort()
+        first = out.to_host()
+        ref_bad = oracle.matmul(bad, b)
+        assert np.array_equal(np.isnan(first), np.isnan(ref_bad))
+        assert np.array_equal(np.isinf(first), np.isinf(ref_bad))
+        da.copy_from_host(a)
+        g.replay()
+        g.quiesce_or_abort()
+        g.replay()
+        g.quiesce_or_abort()
+        second = out.to_host()
+    assert np.isfinite(second).all()
+    assert rel_frob(second, oracle.matmul(a, b)) <= STRICT_TOL
+
+
 def test_vector_operands(oracle):
     a = rng.randn((300,), 1)
     b = rng.randn((300, 40), 2)
