@@ -168,6 +168,41 @@ MMR_API const char *mmr_version(void);
  * read back (MMR_ERR_TIMEOUT is the expected, healthy answer). */
 MMR_API int32_t mmr_selftest_bounded_wait(int32_t device_ordinal, uint64_t limit_ns);
 
+/* ---- one-shot launch that allocates nothing --------------------------------
+ * No counterpart in the reference: the reference's CPU provider never touches
+ * device memory. This is for callers that cannot call cudaMalloc at the point
+ * where they launch -- a serving runtime whose allocator owns every byte of
+ * HBM and forbids other allocations, code that must not pay cudaMalloc's
+ * implicit device synchronisation, or a caller that has no place to keep a
+ * bound handle. mmr_gemm_bind allocates a small scratch area (the kernel's
+ * error word and its bookkeeping for inf/NaN tiles); this entry point uses a
+ * fixed array compiled into the library instead, so it makes no device
+ * allocation at all. Each GPU that loads the library holds that array
+ * (MMR_NOALLOC_SCRATCH_BYTES) until the process exits.
+ *
+ * It validates `desc` exactly as mmr_gemm_bind does, then enqueues the
+ * StrictFp32 (3xTF32) tcgen05 kernel and its inf/NaN fix-up on desc->stream.
+ * Only math_mode MMR_MATH_STRICT_FP32 with a TMA-admissible layout is
+ * accepted, and at most MMR_NOALLOC_MAX_TILES output tiles of 128 x 256
+ * (batch included; 8192 x 8192 needs 2048). Larger problems are rejected with
+ * MMR_ERR_INVALID_SHAPE before anything is launched.
+ *
+ * The first call on a device looks up the array's device address and sets the
+ * kernel's shared-memory limit for that device; make that first call before
+ * any stream capture begins. All calls on a device share the one array: calls
+ * whose work may overlap on the GPU (different streams with no ordering
+ * between them) race on it and must be serialised by the caller. The array
+ * keeps the last call's contents; each call clears the parts that must start
+ * at zero before its kernels run.
+ *
+ * `status_out` (optional, host memory the caller keeps alive until the stream
+ * has passed this call's work; pinned memory keeps the copy asynchronous)
+ * receives 0, or the kernel's device error code when a bounded wait expired.
+ * Returns MMR_OK when the work was enqueued. */
+#define MMR_NOALLOC_SCRATCH_BYTES (64 * 1024)
+#define MMR_NOALLOC_MAX_TILES 8189
+MMR_API int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc *desc, int32_t *status_out);
+
 /* ---- column-block sharding -------------------------------------------------
  * Column range [col0, col1) of rank `rank` when N output columns are dealt to
  * `nranks` ranks in whole units of `align` columns (the output-tile width).

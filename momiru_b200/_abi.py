@@ -34,8 +34,10 @@ FAMILY_NAMES = {FAMILY_AUTO: "auto", FAMILY_TCGEN05: "tcgen05", FAMILY_GEMV: "ge
 EXPORTED = [
     "mmr_gemm_validate", "mmr_gemm_bind", "mmr_gemm_run", "mmr_gemm_run_on", "mmr_gemm_quiesce",
     "mmr_gemm_destroy", "mmr_gemm_query", "mmr_last_error", "mmr_version",
-    "mmr_selftest_bounded_wait", "mmr_shard_columns",
+    "mmr_selftest_bounded_wait", "mmr_shard_columns", "mmr_gemm_run_noalloc",
 ]
+NOALLOC_SCRATCH_BYTES = 64 * 1024
+NOALLOC_MAX_TILES = 8189
 
 
 class MmrView(ctypes.Structure):
@@ -120,6 +122,7 @@ def load() -> ctypes.CDLL:
     lib.mmr_last_error.restype = ctypes.c_char_p
     lib.mmr_version.restype = ctypes.c_char_p
     lib.mmr_selftest_bounded_wait.argtypes = [ctypes.c_int32, ctypes.c_uint64]
+    lib.mmr_gemm_run_noalloc.argtypes = [P(MmrMatmulDesc), P(ctypes.c_int32)]
     lib.mmr_shard_columns.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       P(ctypes.c_int64), P(ctypes.c_int64)]
     for name in EXPORTED:

@@ -587,6 +587,62 @@ int32_t fill_validate_info(const Plan& p, mmr_gemm_info* info) {
 
 // ------------------------------------------------------------------- ABI --
 
+// ------------------------------------------------------------------------
+// Scratch for mmr_gemm_run_noalloc: a fixed array in the library image, so
+// that entry point never allocates device memory. Layout (32-bit words):
+//   [0] device error word, [1..3] unused,
+//   [4] inf/NaN tile count, [5] fix-up blocks done,
+//   [6, 6+T) per-tile flags, [6+T, 6+2T) flagged tile list (T = output tiles).
+// Host code must not use the array's name as a pointer: it stands for a host
+// shadow, not a device address. The device address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+constexpr int kNoAllocWords = MMR_NOALLOC_SCRATCH_BYTES / 4;
+static_assert(6 + 2 * MMR_NOALLOC_MAX_TILES <= kNoAllocWords, "scratch too small for the stated tile limit");
+static __device__ __align__(256) unsigned int g_noalloc_scratch[kNoAllocWords];
+
+namespace {
+
+struct NoAllocDevice {
+  bool ready = false;
+  unsigned int* scratch = nullptr;  // device address of g_noalloc_scratch
+  int sms = 0;
+};
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+
+// First use on a device (that device current): resolve the array's device
+// address and prepare the four 3xTF32 kernel variants (shared-memory opt-in and
+// the register-split check). Allocates nothing.
+int32_t noalloc_setup(int dev, NoAllocDevice** out) {
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "device ordinal %d outside 0..%d", dev, kNoAllocMaxDevices - 1);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  if (!d.ready) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return fail(MMR_ERR_CUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return fail(MMR_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    const int smem = mmr::TcConfig<1>::kSmemBytes;
+    for (int amn = 0; amn < 2; ++amn)
+      for (int bmn = 0; bmn < 2; ++bmn) {
+        e = tc_prep_table(1, amn, bmn)(smem);
+        if (e != cudaSuccess)
+          return fail(MMR_ERR_CUDA, "preparing the 3xTF32 kernel: %s", cudaGetErrorString(e));
+      }
+    d.scratch = static_cast<unsigned int*>(ptr);
+    d.sms = sms;
+    d.ready = true;
+  }
+  *out = &d;
+  return MMR_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* mmr_last_error(void) { return g_last_error.c_str(); }
@@ -915,6 +971,112 @@ int32_t mmr_shard_columns(int64_t n, int32_t nranks, int32_t rank, int32_t align
   const int64_t u1 = u0 + base + (rank < extra ? 1 : 0);
   *col0 = std::min<int64_t>(n, u0 * align);
   *col1 = std::min<int64_t>(n, u1 * align);
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
+  Plan p;
+  int32_t rc = build_plan(desc, &p);
+  if (rc) return rc;
+  if (p.math != MMR_MATH_STRICT_FP32)
+    return fail(MMR_ERR_UNSUPPORTED_MATH, "the allocation-free entry point runs StrictFp32 (3xTF32) only");
+  if (p.family != MMR_FAMILY_AUTO && p.family != MMR_FAMILY_TCGEN05)
+    return fail(MMR_ERR_UNSUPPORTED_FAMILY, "the allocation-free entry point runs the tcgen05 family only");
+  const TmaLayout t = tma_admission(p);
+  if (p.empty) {
+    if (status_out) *status_out = 0;
+    return MMR_OK;
+  }
+  if (!t.ok) return fail(MMR_ERR_UNSUPPORTED_FAMILY, "tcgen05 family not admissible: %s", t.why);
+  const int64_t batch = p.batch0 * p.batch1;
+  const int64_t tiles_m = (p.m + mmr::TC_BM - 1) / mmr::TC_BM;
+  const int64_t tiles_n = (p.n + mmr::TC_BN - 1) / mmr::TC_BN;
+  const int64_t tiles = tiles_m * tiles_n * batch;
+  if (tiles > MMR_NOALLOC_MAX_TILES)
+    return fail(MMR_ERR_INVALID_SHAPE,
+                "output needs %lld tiles of 128x256; the allocation-free entry point's static scratch "
+                "(%d bytes) holds at most %d",
+                (long long)tiles, MMR_NOALLOC_SCRATCH_BYTES, MMR_NOALLOC_MAX_TILES);
+
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "no CUDA device is visible");
+  if (p.device < 0 || p.device >= ndev)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "device ordinal %d outside 0..%d", p.device, ndev - 1);
+  DeviceGuard guard(p.device);
+  if (!guard.ok) return fail(MMR_ERR_CUDA, "cudaSetDevice(%d) failed", p.device);
+  int major = 0;
+  MMR_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, p.device));
+  if (major != 10) return fail(MMR_ERR_UNSUPPORTED_DEVICE, "device %d is not an sm_100 device", p.device);
+  const uint64_t addrs[4] = {desc->lhs.address, desc->rhs.address, desc->out.address,
+                             (desc->epilogue == MMR_EPI_BIAS || desc->epilogue == MMR_EPI_BIAS_RELU) ? desc->bias.address : 0};
+  for (uint64_t a : addrs) {
+    if (!a) continue;
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, reinterpret_cast<void*>(a)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(MMR_ERR_UNSUPPORTED_DEVICE, "address 0x%llx is not known to CUDA", (unsigned long long)a);
+    }
+    if ((pa.type != cudaMemoryTypeDevice && pa.type != cudaMemoryTypeManaged) || pa.device != p.device)
+      return fail(MMR_ERR_UNSUPPORTED_DEVICE, "address 0x%llx is not device memory of device %d",
+                  (unsigned long long)a, p.device);
+  }
+  NoAllocDevice* dev = nullptr;
+  if ((rc = noalloc_setup(p.device, &dev))) return rc;
+
+  // Everything below lives on the stack: descriptors, parameters, launch shape.
+  mmr_gemm_handle h;
+  h.plan = p;
+  h.device = p.device;
+  h.mode = 1;
+  h.a_mn = t.a_mn;
+  h.b_mn = t.b_mn;
+  int32_t e;
+  if (!t.a_mn) e = encode_3d(&h.tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, 32, mmr::TC_BM, "lhs");
+  else e = encode_3d(&h.tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, 32, "lhs", true);
+  if (e) return e;
+  if (t.b_mn) e = encode_3d(&h.tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, 32, "rhs", true);
+  else e = encode_3d(&h.tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, 32, mmr::TC_BN, "rhs");
+  if (e) return e;
+  if ((e = encode_3d(&h.tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out"))) return e;
+
+  mmr::TcParams& q = h.tcp;
+  q.m = int(p.m);
+  q.n = int(p.n);
+  q.k = int(p.k);
+  q.batch = int(batch);
+  q.tiles_m = int(tiles_m);
+  q.tiles_n = int(tiles_n);
+  q.tiles_total = int(tiles);
+  q.k_blocks = int((p.k + mmr::TC_BK - 1) / mmr::TC_BK);
+  q.chunk_kb = 8;
+  q.a_batched = t.a_batched;
+  q.b_batched = t.b_batched;
+  q.epilogue = p.epilogue;
+  q.bias = reinterpret_cast<const float*>(p.bias);
+  q.c = reinterpret_cast<float*>(p.c.base);
+  q.c_ld = p.c.s_r;
+  q.c_bs = t.c_sb;
+  q.err = reinterpret_cast<int*>(dev->scratch);
+  q.timeout_ns = h.wait_timeout_ns;
+  q.nf = dev->scratch + 4;
+  fill_simt_params(p, &h.sp);
+  h.smem = mmr::TcConfig<1>::kSmemBytes;
+  h.grid = dim3(unsigned(std::min<int64_t>(tiles, dev->sms)));
+  h.block = dim3(mmr::TcConfig<1>::kThreads);
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(desc->stream);
+  // Clear what the kernels expect at zero: the error word, the flagged-tile
+  // count and done counter, and this problem's per-tile flags.
+  MMR_CUDA_TRY(cudaMemsetAsync(dev->scratch, 0, (6 + size_t(tiles)) * sizeof(unsigned int), s));
+  cudaError_t ce = tc_launch_table(1, t.a_mn, t.b_mn)(&h, s);
+  if (ce == cudaSuccess) {
+    mmr::tc_nonfinite_fixup_kernel<<<dev->sms, 256, 0, s>>>(h.sp, h.tcp);
+    ce = cudaGetLastError();
+  }
+  if (ce != cudaSuccess) return fail(MMR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(ce));
+  if (status_out)
+    MMR_CUDA_TRY(cudaMemcpyAsync(status_out, dev->scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
   return MMR_OK;
 }
 
