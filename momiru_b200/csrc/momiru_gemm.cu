@@ -366,6 +366,9 @@ EncodeTiledFn encode_fn() {
 int32_t encode_3d(CUtensorMap* tm, uint64_t base, uint64_t inner, uint64_t outer, uint64_t batch,
                   int64_t outer_stride_el, int64_t batch_stride_el, uint32_t box_inner, uint32_t box_outer,
                   const char* name, bool atom32 = false) {
+  // A 16-wide (64-byte) box of a K-major operand takes the 64-byte swizzle.
+  const CUtensorMapSwizzle swz = atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                 : box_inner * 4 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(MMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   if (batch < 1) batch = 1;
@@ -380,8 +383,7 @@ int32_t encode_3d(CUtensorMap* tm, uint64_t base, uint64_t inner, uint64_t outer
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, reinterpret_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -422,6 +424,20 @@ struct mmr_gemm_handle {
 };
 
 namespace {
+
+// The three tensor maps of a tcgen05 launch: operand boxes are one k-block
+// wide (bk = 32 or 16 f32) and 128 (A) / 256 (B) long, or 32-wide MN atoms;
+// the output box is 32 x 32.
+int32_t encode_tc_maps(mmr_gemm_handle* h, const Plan& p, const TmaLayout& t, int64_t batch, uint32_t bk) {
+  int32_t e;
+  if (!t.a_mn) e = encode_3d(&h->tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, bk, mmr::TC_BM, "lhs");
+  else e = encode_3d(&h->tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, bk, "lhs", true);
+  if (e) return e;
+  if (t.b_mn) e = encode_3d(&h->tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, bk, "rhs", true);
+  else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, bk, mmr::TC_BN, "rhs");
+  if (e) return e;
+  return encode_3d(&h->tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out");
+}
 
 template <int MODE, bool AMN, bool BMN>
 cudaError_t launch_tc(mmr_gemm_handle* h, cudaStream_t s) {
@@ -732,17 +748,8 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     h->mode = (p.math == MMR_MATH_STRICT_FP32) ? 1 : 0;
     h->a_mn = t.a_mn;
     h->b_mn = t.b_mn;
-    int32_t e;
-    // A
-    if (!t.a_mn) e = encode_3d(&h->tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, 32, mmr::TC_BM, "lhs");
-    else e = encode_3d(&h->tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, 32, "lhs", true);
-    if (e) return cleanup(e);
-    // B
-    if (t.b_mn) e = encode_3d(&h->tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, 32, "rhs", true);
-    else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, 32, mmr::TC_BN, "rhs");
-    if (e) return cleanup(e);
-    // C
-    e = encode_3d(&h->tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out");
+    const uint32_t bk = h->mode ? mmr::TcConfig<1>::kBK : mmr::TcConfig<0>::kBK;
+    int32_t e = encode_tc_maps(h, p, t, batch, bk);
     if (e) return cleanup(e);
 
     mmr::TcParams& q = h->tcp;
@@ -755,10 +762,10 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     const int64_t tiles = int64_t(q.tiles_m) * q.tiles_n * batch;
     if (tiles > INT32_MAX) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "too many output tiles"));
     q.tiles_total = int(tiles);
-    q.k_blocks = int((p.k + mmr::TC_BK - 1) / mmr::TC_BK);
-    // StrictFp32 sums K in chunks of 256 (8 k-blocks) with round-to-nearest
-    // adds; one TF32 pass keeps a single chain per tile.
-    q.chunk_kb = h->mode ? 8 : q.k_blocks;
+    q.k_blocks = int((p.k + bk - 1) / bk);
+    // StrictFp32 sums K in chunks of 256 with round-to-nearest adds; one TF32
+    // pass keeps a single chain per tile.
+    q.chunk_kb = h->mode ? int(256 / bk) : q.k_blocks;
     q.c = reinterpret_cast<float*>(p.c.base);
     q.c_ld = p.c.s_r;
     q.c_bs = t.c_sb;
@@ -789,7 +796,7 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     h->info.b_mn_major = t.b_mn;
     h->info.tile_m = mmr::TC_BM;
     h->info.tile_n = mmr::TC_BN;
-    h->info.tile_k = mmr::TC_BK;
+    h->info.tile_k = int(bk);
     h->info.stages = h->mode ? mmr::TcConfig<1>::kStages : mmr::TcConfig<0>::kStages;
     h->info.tiles = tiles;
     h->info.bytes = algorithmic_bytes(p, t.a_batched, t.b_batched);
@@ -1031,14 +1038,8 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   h.mode = 1;
   h.a_mn = t.a_mn;
   h.b_mn = t.b_mn;
-  int32_t e;
-  if (!t.a_mn) e = encode_3d(&h.tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, 32, mmr::TC_BM, "lhs");
-  else e = encode_3d(&h.tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, 32, "lhs", true);
-  if (e) return e;
-  if (t.b_mn) e = encode_3d(&h.tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, 32, "rhs", true);
-  else e = encode_3d(&h.tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, 32, mmr::TC_BN, "rhs");
-  if (e) return e;
-  if ((e = encode_3d(&h.tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out"))) return e;
+  constexpr uint32_t bk = mmr::TcConfig<1>::kBK;
+  if (int32_t e = encode_tc_maps(&h, p, t, batch, bk)) return e;
 
   mmr::TcParams& q = h.tcp;
   q.m = int(p.m);
@@ -1048,8 +1049,8 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   q.tiles_m = int(tiles_m);
   q.tiles_n = int(tiles_n);
   q.tiles_total = int(tiles);
-  q.k_blocks = int((p.k + mmr::TC_BK - 1) / mmr::TC_BK);
-  q.chunk_kb = 8;
+  q.k_blocks = int((p.k + bk - 1) / bk);
+  q.chunk_kb = int(256 / bk);
   q.a_batched = t.a_batched;
   q.b_batched = t.b_batched;
   q.epilogue = p.epilogue;

@@ -12,15 +12,16 @@
 //               f32 registers with round-to-nearest adds, then +bias, ReLU,
 //               swizzled shared staging and a TMA store (clipped at the
 //               tensor edge; a ragged right edge uses guarded plain stores)
-//   warp 8      producer: TMA loads of A/B k-blocks into an S-stage ring
+//   warp 8      producer: TMA loads of A/B k-blocks into a 4-stage ring
 //   warp 9      MMA issuer: tcgen05.mma kind::tf32 into two TMEM partial
 //               accumulators of 256 columns, alternating per K-chunk
-//   warps 10-15 (3xTF32 only) split: each staged f32 operand x becomes
-//               hi = x with the low 13 mantissa bits cleared (exact in TF32)
-//               and lo = x - hi (exact in f32); the MMA issuer then runs
+//   warps 10-15 (3xTF32 only) split: for each staged f32 operand x, hi is x
+//               with the low 13 mantissa bits cleared -- exactly what the
+//               tensor core reads from x itself -- and lo = x - hi (exact in
+//               f32) is written beside it; the MMA issuer then runs
 //               lo*hi + hi*lo + hi*hi per k-step (the error-corrected TF32
 //               method of Ootomo & Yokota, 2022).
-// K is accumulated in chunks of `chunk_kb` k-blocks: the tensor core's f32
+// K is accumulated in chunks of `chunk_kb` k-blocks (256 wide in 3xTF32): the tensor core's f32
 // accumulation is not round-to-nearest, so a single 8192-long chain drifts by
 // ~6e-5 relative; short chains summed with RN adds stay near 2e-6.
 // Every wait is bounded; on expiry the kernel records an error word, drains
@@ -38,10 +39,6 @@ namespace mmr {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BN = 256;
-constexpr int TC_BK = 32;  // 32 f32 = 128 bytes = one 128-byte swizzle row
-constexpr int TC_A_BYTES = TC_BM * TC_BK * 4;   // 16 KiB
-constexpr int TC_B_BYTES = TC_BN * TC_BK * 4;   // 32 KiB
-constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;
 constexpr int TC_CSTAGE_BYTES = 32 * 32 * 4;    // one 32x32 f32 store box
 constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_PRODUCER_WARP = 8;
@@ -52,9 +49,16 @@ constexpr int TC_GROUP_M = 16;                  // tile raster: M-tiles per grou
 
 enum : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU = 3 };
 
+// Per-mode tile geometry. TF32 stages 32-wide k-blocks (128-byte rows); 3xTF32
+// stages 16-wide k-blocks (64-byte rows) so that four stages of raw + split
+// operands fit in shared memory and cover the TMA latency.
 template <int MODE>
 struct TcConfig {
-  static constexpr int kStages = MODE ? 2 : 4;
+  static constexpr int kBK = MODE ? 16 : 32;
+  static constexpr int kABytes = TC_BM * kBK * 4;
+  static constexpr int kBBytes = TC_BN * kBK * 4;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = 4;
   static constexpr int kWarps = MODE ? 16 : 12;
   static constexpr int kThreads = 32 * kWarps;
   // Register split by warpgroup (setmaxnreg): the two epilogue warpgroups
@@ -64,7 +68,17 @@ struct TcConfig {
   static constexpr int kLaunchRegs = MODE ? 128 : 168;
   static constexpr int kEpiRegs = MODE ? 176 : 200;
   static constexpr int kOtherRegs = MODE ? 80 : 96;
-  static constexpr int kOperandBytes = kStages * TC_STAGE_BYTES * (MODE ? 2 : 1);
+  static constexpr int kOperandBytes = kStages * kStageBytes * (MODE ? 2 : 1);
+  // Shared-memory descriptor geometry (bytes):
+  //  K-major: rows of kBK*4 bytes swizzled with 16-byte atoms (layout 2 for
+  //  128-byte rows, 4 for 64-byte rows), 8-row groups kRow*8 apart (SBO),
+  //  +32 B per 8-wide k-step.
+  //  MN-major tf32 must use the 128-byte swizzle with 32-byte atoms (layout 1,
+  //  TMA SWIZZLE_128B_ATOM_32B): 32-element MN atoms kBK*128 apart (LBO),
+  //  4-row K groups 512 B apart (SBO), +1024 B per 8-wide k-step.
+  static constexpr uint32_t kKmajLayout = kBK == 32 ? 2u : 4u;
+  static constexpr uint32_t kKmajSbo = 8u * kBK * 4u;
+  static constexpr uint32_t kMnAtomBytes = kBK * 128u;
   static constexpr int kCstageBytes = TC_EPI_WARPS * TC_CSTAGE_BYTES;
   static constexpr int kBarrierBytes = 256;
   // +1024 so the kernel can round its dynamic base up to 1024 bytes.
@@ -123,7 +137,7 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ops = smem;                                     // [S][A|B]
-  uint8_t* lo_ops = smem + S * TC_STAGE_BYTES;             // [S][Alo|Blo] (3xTF32)
+  uint8_t* lo_ops = smem + S * Cfg::kStageBytes;             // [S][Alo|Blo] (3xTF32)
   uint8_t* cstage = smem + Cfg::kOperandBytes;             // [8 warps][32x32]
   uint64_t* bars = reinterpret_cast<uint64_t*>(cstage + Cfg::kCstageBytes);
   uint64_t* full = bars;             // [S] TMA -> split/MMA
@@ -263,21 +277,21 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
           const int ba = p.a_batched ? bt : 0, bb = p.b_batched ? bt : 0;
           for (int kb = 0; kb < p.k_blocks; ++kb) {
             if (!mbar_wait(&empty[stage], phase ^ 1u, ctl, kDevTimeoutEmpty)) { ok = false; break; }
-            uint8_t* sa = ops + stage * TC_STAGE_BYTES;
-            uint8_t* sb = sa + TC_A_BYTES;
-            const int k0 = kb * TC_BK;
-            mbar_arrive_expect_tx(&full[stage], TC_STAGE_BYTES);
+            uint8_t* sa = ops + stage * Cfg::kStageBytes;
+            uint8_t* sb = sa + Cfg::kABytes;
+            const int k0 = kb * Cfg::kBK;
+            mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
             if (A_MN) {
 #pragma unroll
               for (int i = 0; i < TC_BM / 32; ++i)
-                tma_load_3d(sa + i * 4096, &tmA, &full[stage], m0 + 32 * i, k0, ba);
+                tma_load_3d(sa + i * Cfg::kMnAtomBytes, &tmA, &full[stage], m0 + 32 * i, k0, ba);
             } else {
               tma_load_3d(sa, &tmA, &full[stage], k0, m0, ba);
             }
             if (B_MN) {
 #pragma unroll
               for (int j = 0; j < TC_BN / 32; ++j)
-                tma_load_3d(sb + j * 4096, &tmB, &full[stage], n0 + 32 * j, k0, bb);
+                tma_load_3d(sb + j * Cfg::kMnAtomBytes, &tmB, &full[stage], n0 + 32 * j, k0, bb);
             } else {
               tma_load_3d(sb, &tmB, &full[stage], k0, n0, bb);
             }
@@ -301,15 +315,11 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
       // -------------------------------------------------------- MMA issuer
       if (lane == 0) {
         constexpr uint32_t idesc = idesc_tf32(TC_BM, TC_BN, A_MN, B_MN);
-        // Descriptor geometry (bytes).
-        //  K-major, 128-byte swizzle (layout 2, 16-byte atoms): rows of 128 B,
-        //  8-row groups 1024 B apart (SBO), +32 B per 8-wide k-step.
-        //  MN-major tf32 must use the 128-byte swizzle with 32-byte atoms
-        //  (layout 1, TMA SWIZZLE_128B_ATOM_32B): 32-element MN atoms 4096 B
-        //  apart (LBO), 4-row K groups 512 B apart (SBO), +1024 B per k-step.
-        constexpr uint32_t a_layout = A_MN ? 1u : 2u, b_layout = B_MN ? 1u : 2u;
-        constexpr uint32_t a_lbo = A_MN ? 4096u : 16u, a_sbo = A_MN ? 512u : 1024u, a_kstep = A_MN ? 1024u : 32u;
-        constexpr uint32_t b_lbo = B_MN ? 4096u : 16u, b_sbo = B_MN ? 512u : 1024u, b_kstep = B_MN ? 1024u : 32u;
+        // Descriptor geometry: see TcConfig.
+        constexpr uint32_t a_layout = A_MN ? 1u : Cfg::kKmajLayout, b_layout = B_MN ? 1u : Cfg::kKmajLayout;
+        constexpr uint32_t a_lbo = A_MN ? Cfg::kMnAtomBytes : 16u, a_sbo = A_MN ? 512u : Cfg::kKmajSbo;
+        constexpr uint32_t b_lbo = B_MN ? Cfg::kMnAtomBytes : 16u, b_sbo = B_MN ? 512u : Cfg::kKmajSbo;
+        constexpr uint32_t a_kstep = A_MN ? 1024u : 32u, b_kstep = B_MN ? 1024u : 32u;
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
@@ -328,12 +338,12 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
             uint64_t* ready = MODE ? &split_done[stage] : &full[stage];
             if (!mbar_wait(ready, phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sa = smem_u32(ops + stage * TC_STAGE_BYTES);
-            const uint32_t sb = sa + TC_A_BYTES;
-            const uint32_t sa_lo = smem_u32(lo_ops + stage * TC_STAGE_BYTES);
-            const uint32_t sb_lo = sa_lo + TC_A_BYTES;
+            const uint32_t sa = smem_u32(ops + stage * Cfg::kStageBytes);
+            const uint32_t sb = sa + Cfg::kABytes;
+            const uint32_t sa_lo = smem_u32(lo_ops + stage * Cfg::kStageBytes);
+            const uint32_t sb_lo = sa_lo + Cfg::kABytes;
 #pragma unroll
-            for (int kk = 0; kk < TC_BK / 8; ++kk) {
+            for (int kk = 0; kk < Cfg::kBK / 8; ++kk) {
               const uint64_t ad = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_layout);
               const uint64_t bd = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_layout);
               const uint32_t accumulate = (kc | kk) != 0;
@@ -376,28 +386,26 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
       for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, ctl, kDevTimeoutFull)) { ok = false; break; }
-          uint4* x = reinterpret_cast<uint4*>(ops + stage * TC_STAGE_BYTES);
-          uint4* lo = reinterpret_cast<uint4*>(lo_ops + stage * TC_STAGE_BYTES);
+          uint4* x = reinterpret_cast<uint4*>(ops + stage * Cfg::kStageBytes);
+          uint4* lo = reinterpret_cast<uint4*>(lo_ops + stage * Cfg::kStageBytes);
           bool nonfinite = false;
+          // The tensor core reads an f32 operand as TF32 by dropping its low 13
+          // mantissa bits, so the staged raw value already is hi; only
+          // lo = x - hi is written. Tiles with inf/NaN are flagged and
+          // recomputed exactly by the fix-up kernel.
 #pragma unroll 4
-          for (int i = tid; i < TC_STAGE_BYTES / 16; i += TC_SPLIT_WARPS * 32) {
-            uint4 v = x[i];
-            uint4 h, l;
-#define MMR_SPLIT1(F)                                                                     \
-  {                                                                                       \
-    const uint32_t u = v.F;                                                               \
-    if ((u & 0x7F800000u) == 0x7F800000u) {                                               \
-      h.F = (u & 0x007FFFFFu) ? 0x7FC00000u : u;                                          \
-      l.F = 0u;                                                                           \
-      nonfinite = true;                                                                   \
-    } else {                                                                              \
-      h.F = u & 0xFFFFE000u;                                                              \
-      l.F = __float_as_uint(__fsub_rn(__uint_as_float(u), __uint_as_float(h.F)));        \
-    }                                                                                     \
+          for (int i = tid; i < Cfg::kStageBytes / 16; i += TC_SPLIT_WARPS * 32) {
+            const uint4 v = x[i];
+            uint4 l;
+#define MMR_SPLIT1(F)                                                                        \
+  {                                                                                          \
+    const uint32_t u = v.F;                                                                  \
+    const bool nf = (u & 0x7F800000u) == 0x7F800000u;                                        \
+    nonfinite |= nf;                                                                         \
+    l.F = nf ? 0u : __float_as_uint(__fsub_rn(__uint_as_float(u), __uint_as_float(u & 0xFFFFE000u))); \
   }
             MMR_SPLIT1(x) MMR_SPLIT1(y) MMR_SPLIT1(z) MMR_SPLIT1(w)
 #undef MMR_SPLIT1
-            x[i] = h;
             lo[i] = l;
           }
           fence_proxy_async_smem();
