@@ -22,6 +22,7 @@
 #include "ptx.cuh"
 #include "simt_gemm.cuh"
 #include "tc_gemm.cuh"
+#include "tc_gemm_2sm.cuh"
 
 namespace {
 
@@ -407,6 +408,7 @@ struct mmr_gemm_handle {
   mmr::TcParams tcp{};
   bool a_mn = false, b_mn = false;
   int mode = 0;
+  bool pair = false;  // StrictFp32 on CTA pairs (cta_group::2)
   // gemv
   mmr::GemvParams gvp{};
   int gv_mt = 16;
@@ -426,15 +428,16 @@ struct mmr_gemm_handle {
 namespace {
 
 // The three tensor maps of a tcgen05 launch: operand boxes are one k-block
-// wide (bk = 32 or 16 f32) and 128 (A) / 256 (B) long, or 32-wide MN atoms;
-// the output box is 32 x 32.
-int32_t encode_tc_maps(mmr_gemm_handle* h, const Plan& p, const TmaLayout& t, int64_t batch, uint32_t bk) {
+// wide (bk = 32 or 16 f32) and 128 (A) / b_rows (B: 256 for one CTA, 128 for
+// each CTA of a pair) long, or 32-wide MN atoms; the output box is 32 x 32.
+int32_t encode_tc_maps(mmr_gemm_handle* h, const Plan& p, const TmaLayout& t, int64_t batch, uint32_t bk,
+                       uint32_t b_rows = mmr::TC_BN) {
   int32_t e;
   if (!t.a_mn) e = encode_3d(&h->tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, bk, mmr::TC_BM, "lhs");
   else e = encode_3d(&h->tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, bk, "lhs", true);
   if (e) return e;
   if (t.b_mn) e = encode_3d(&h->tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, bk, "rhs", true);
-  else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, bk, mmr::TC_BN, "rhs");
+  else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, bk, b_rows, "rhs");
   if (e) return e;
   return encode_3d(&h->tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out");
 }
@@ -463,6 +466,37 @@ cudaError_t prepare_tc(int smem) {
   return cudaSuccess;
 }
 
+template <bool AMN, bool BMN>
+cudaError_t launch_tc2(mmr_gemm_handle* h, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = h->grid;
+  cfg.blockDim = h->block;
+  cfg.dynamicSmemBytes = h->smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, mmr::tc_gemm_2sm_kernel<AMN, BMN>, h->tmA, h->tmB, h->tmC, h->tcp);
+}
+
+template <bool AMN, bool BMN>
+cudaError_t prepare_tc2(int smem) {
+  using Cfg = mmr::Tc2Config;
+  cudaError_t e = cudaFuncSetAttribute(mmr::tc_gemm_2sm_kernel<AMN, BMN>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, mmr::tc_gemm_2sm_kernel<AMN, BMN>);
+  if (e != cudaSuccess) return e;
+  const long need = 2L * 128 * Cfg::kEpiRegs + long(Cfg::kThreads - 256) * Cfg::kOtherRegs;
+  if (long(fa.numRegs) * Cfg::kThreads < need) return cudaErrorInvalidConfiguration;
+  return cudaSuccess;
+}
+
 using TcLaunch = cudaError_t (*)(mmr_gemm_handle*, cudaStream_t);
 using TcPrep = cudaError_t (*)(int);
 
@@ -472,6 +506,17 @@ TcLaunch tc_launch_table(int mode, bool amn, bool bmn) {
       {{launch_tc<1, false, false>, launch_tc<1, false, true>}, {launch_tc<1, true, false>, launch_tc<1, true, true>}}};
   return t[mode][amn][bmn];
 }
+TcLaunch tc2_launch_table(bool amn, bool bmn) {
+  static const TcLaunch t[2][2] = {{launch_tc2<false, false>, launch_tc2<false, true>},
+                                   {launch_tc2<true, false>, launch_tc2<true, true>}};
+  return t[amn][bmn];
+}
+TcPrep tc2_prep_table(bool amn, bool bmn) {
+  static const TcPrep t[2][2] = {{prepare_tc2<false, false>, prepare_tc2<false, true>},
+                                 {prepare_tc2<true, false>, prepare_tc2<true, true>}};
+  return t[amn][bmn];
+}
+
 TcPrep tc_prep_table(int mode, bool amn, bool bmn) {
   static const TcPrep t[2][2][2] = {
       {{prepare_tc<0, false, false>, prepare_tc<0, false, true>}, {prepare_tc<0, true, false>, prepare_tc<0, true, true>}},
@@ -746,10 +791,14 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
   const int64_t batch = p.batch0 * p.batch1;
   if (fam == MMR_FAMILY_TCGEN05) {
     h->mode = (p.math == MMR_MATH_STRICT_FP32) ? 1 : 0;
+    // StrictFp32 runs on CTA pairs (256-row tiles) unless M fits one 128-row tile.
+    h->pair = h->mode == 1 && p.m > mmr::TC_BM;
     h->a_mn = t.a_mn;
     h->b_mn = t.b_mn;
-    const uint32_t bk = h->mode ? mmr::TcConfig<1>::kBK : mmr::TcConfig<0>::kBK;
-    int32_t e = encode_tc_maps(h, p, t, batch, bk);
+    const uint32_t bk = h->pair ? uint32_t(mmr::Tc2Config::kBK)
+                                : (h->mode ? mmr::TcConfig<1>::kBK : mmr::TcConfig<0>::kBK);
+    const int tile_m = h->pair ? 2 * mmr::TC_BM : mmr::TC_BM;
+    int32_t e = encode_tc_maps(h, p, t, batch, bk, h->pair ? 128u : uint32_t(mmr::TC_BN));
     if (e) return cleanup(e);
 
     mmr::TcParams& q = h->tcp;
@@ -757,7 +806,8 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     q.n = int(p.n);
     q.k = int(p.k);
     q.batch = int(batch);
-    q.tiles_m = int((p.m + mmr::TC_BM - 1) / mmr::TC_BM);
+    q.tile_m = tile_m;
+    q.tiles_m = int((p.m + tile_m - 1) / tile_m);
     q.tiles_n = int((p.n + mmr::TC_BN - 1) / mmr::TC_BN);
     const int64_t tiles = int64_t(q.tiles_m) * q.tiles_n * batch;
     if (tiles > INT32_MAX) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "too many output tiles"));
@@ -785,19 +835,30 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
       fill_simt_params(p, &h->sp);
     }
     h->sms = sms;
-    h->smem = h->mode ? mmr::TcConfig<1>::kSmemBytes : mmr::TcConfig<0>::kSmemBytes;
-    h->grid = dim3(unsigned(std::min<int64_t>(tiles, sms)));
-    h->block = dim3(h->mode ? mmr::TcConfig<1>::kThreads : mmr::TcConfig<0>::kThreads);
-    cudaError_t ce = tc_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
+    cudaError_t ce;
+    if (h->pair) {
+      h->smem = mmr::Tc2Config::kSmemBytes;
+      h->grid = dim3(unsigned(2 * std::min<int64_t>(tiles, sms / 2)));
+      h->block = dim3(mmr::Tc2Config::kThreads);
+      ce = tc2_prep_table(t.a_mn, t.b_mn)(h->smem);
+      h->info.cluster = 2;
+      h->info.stages = mmr::Tc2Config::kStages;
+    } else {
+      h->smem = h->mode ? mmr::TcConfig<1>::kSmemBytes : mmr::TcConfig<0>::kSmemBytes;
+      h->grid = dim3(unsigned(std::min<int64_t>(tiles, sms)));
+      h->block = dim3(h->mode ? mmr::TcConfig<1>::kThreads : mmr::TcConfig<0>::kThreads);
+      ce = tc_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
+      h->info.cluster = 1;
+      h->info.stages = h->mode ? mmr::TcConfig<1>::kStages : mmr::TcConfig<0>::kStages;
+    }
     if (ce == cudaErrorInvalidConfiguration)
       return cleanup(fail(MMR_ERR_CUDA, "tcgen05 kernel was compiled with too few registers for its warp split"));
     if (ce != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce)));
     h->info.a_mn_major = t.a_mn;
     h->info.b_mn_major = t.b_mn;
-    h->info.tile_m = mmr::TC_BM;
+    h->info.tile_m = tile_m;
     h->info.tile_n = mmr::TC_BN;
     h->info.tile_k = int(bk);
-    h->info.stages = h->mode ? mmr::TcConfig<1>::kStages : mmr::TcConfig<0>::kStages;
     h->info.tiles = tiles;
     h->info.bytes = algorithmic_bytes(p, t.a_batched, t.b_batched);
   } else if (fam == MMR_FAMILY_GEMV) {
@@ -854,7 +915,7 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
   if (!h->plan.empty) {
     switch (h->family) {
       case MMR_FAMILY_TCGEN05:
-        e = tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s);
+        e = h->pair ? tc2_launch_table(h->a_mn, h->b_mn)(h, s) : tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s);
         if (e == cudaSuccess && h->mode == 1) {
           mmr::tc_nonfinite_fixup_kernel<<<h->sms, 256, 0, s>>>(h->sp, h->tcp);
           e = cudaGetLastError();
@@ -1046,6 +1107,7 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   q.n = int(p.n);
   q.k = int(p.k);
   q.batch = int(batch);
+  q.tile_m = mmr::TC_BM;
   q.tiles_m = int(tiles_m);
   q.tiles_n = int(tiles_n);
   q.tiles_total = int(tiles);

@@ -90,6 +90,7 @@ struct TcConfig {
 struct TcParams {
   int m, n, k;
   int batch;
+  int tile_m;                // output tile height: 128 (one CTA) or 256 (CTA pair)
   int tiles_m, tiles_n;
   int tiles_total;
   int k_blocks;
@@ -436,13 +437,13 @@ __global__ void __launch_bounds__(256) tc_nonfinite_fixup_kernel(const SimtParam
   __shared__ bool last;
   const unsigned int count = *reinterpret_cast<volatile unsigned int*>(&p.nf[0]);
   if (count == 0) return;
-  constexpr int kSub = (TC_BM / SIMT_BM) * (TC_BN / SIMT_BN);
+  const int kSub = (p.tile_m / SIMT_BM) * (TC_BN / SIMT_BN);
   for (unsigned int w = blockIdx.x; w < count * kSub; w += gridDim.x) {
     const int t = static_cast<int>(p.nf[2 + p.tiles_total + w / kSub]);
     const int sub = static_cast<int>(w % kSub);
     int mt, nt, bt;
     tc_tile_coords(p, t, mt, nt, bt);
-    const int m0 = mt * TC_BM + (sub / (TC_BN / SIMT_BN)) * SIMT_BM;
+    const int m0 = mt * p.tile_m + (sub / (TC_BN / SIMT_BN)) * SIMT_BM;
     const int n0 = nt * TC_BN + (sub % (TC_BN / SIMT_BN)) * SIMT_BN;
     simt_block_exact(sp, m0, n0, bt, As, Bs);
   }

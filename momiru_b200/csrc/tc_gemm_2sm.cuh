@@ -1,0 +1,353 @@
+// tc_gemm_2sm.cuh -- 3xTF32 f32 GEMM on CTA pairs (tcgen05 cta_group::2).
+//
+// Same contract and numerics as tc_gemm_kernel<1, ...> (StrictFp32: 3xTF32
+// split, 256-wide K chunks summed with round-to-nearest adds, exact fix-up
+// of tiles with inf/NaN inputs), but each output tile of 256 x 256 is
+// computed by a cluster of two CTAs on two SMs with one 256-row MMA per
+// k-step. Each CTA stages only its 128 rows of A and its 128-column half of
+// B (plus their lo parts), which halves the per-SM shared-memory traffic of
+// the B operand -- the bound of the one-CTA 3xTF32 kernel.
+//
+// Pair protocol (rank 0 = even CTA issues every MMA of the pair):
+//   full[s]        local, TMA -> split warps of the same CTA
+//   split_done[s]  rank 0 only, 12 arrivals: six split warps of each CTA
+//   empty[s]       each CTA, one arrival from rank 0's tcgen05.commit
+//   acc_full[a]    each CTA, one arrival from rank 0's tcgen05.commit
+//   acc_empty[a]   rank 0 only, 16 arrivals: eight epilogue warps of each CTA
+// Commits reach the odd CTA's barriers by their cluster address (no
+// multicast). Both CTAs pass a cluster barrier after set-up and before
+// freeing TMEM.
+#pragma once
+#include "tc_gemm.cuh"
+
+namespace mmr {
+
+struct Tc2Config {
+  static constexpr int kBK = 16;
+  static constexpr int kABytes = 128 * kBK * 4;          // this CTA's 128 rows of A
+  static constexpr int kBBytes = 128 * kBK * 4;          // this CTA's 128 columns of B
+  static constexpr int kStageBytes = kABytes + kBBytes;  // 16 KiB raw (+16 KiB lo)
+  static constexpr int kStages = 6;
+  static constexpr int kWarps = 16;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kLaunchRegs = 128;
+  static constexpr int kEpiRegs = 176;
+  static constexpr int kOtherRegs = 80;
+  static constexpr int kOperandBytes = kStages * kStageBytes * 2;
+  static constexpr int kCstageBytes = TC_EPI_WARPS * TC_CSTAGE_BYTES;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kOperandBytes + kCstageBytes + kBarrierBytes + 1024;
+  static constexpr uint32_t kMnAtomBytes = kBK * 128u;   // 32 MN elements x 16 K rows
+  static_assert(2 * 128 * kEpiRegs + (kWarps - 8) * 32 * kOtherRegs <= kThreads * kLaunchRegs,
+                "register split exceeds the launch budget");
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(Tc2Config::kThreads, 1)
+    tc_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmC, const TcParams p) {
+  using Cfg = Tc2Config;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ops = smem;
+  uint8_t* lo_ops = smem + S * Cfg::kStageBytes;
+  uint8_t* cstage = smem + Cfg::kOperandBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cstage + Cfg::kCstageBytes);
+  uint64_t* full = bars;
+  uint64_t* split_done = bars + S;
+  uint64_t* empty = bars + 2 * S;
+  uint64_t* acc_full = bars + 3 * S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int npairs = static_cast<int>(gridDim.x >> 1);
+  const WaitCtl ctl{p.err, p.timeout_ns};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&split_done[s], 2 * TC_SPLIT_WARPS);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 2 * TC_EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == TC_PRODUCER_WARP && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == TC_MMA_WARP) {
+    tmem_alloc_2sm(tmem_slot, 512);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // barrier inits and both TMEM allocations visible to the pair
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int n_chunks = (p.k_blocks + p.chunk_kb - 1) / p.chunk_kb;
+
+  if (warp < TC_EPI_WARPS) {
+    reg_alloc<Cfg::kEpiRegs>();
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3, half = warp >> 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    uint8_t* buf = cstage + warp * TC_CSTAGE_BYTES;
+    const bool add_bias = (p.epilogue == EPI_BIAS || p.epilogue == EPI_BIAS_RELU);
+    const bool relu = (p.epilogue == EPI_BIAS_RELU || p.epilogue == EPI_RELU);
+    const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    bool ok = true;
+    for (int t = pair; ok && t < p.tiles_total; t += npairs) {
+      int mt, nt, bt;
+      tc_tile_coords(p, t, mt, nt, bt);
+      const int m0 = mt * 256 + static_cast<int>(rank) * 128, n0 = nt * TC_BN;
+      float sum[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) sum[i] = 0.0f;
+      for (int c = 0; c < n_chunks; ++c) {
+        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, ctl, kDevTimeoutAcc)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                            static_cast<uint32_t>(acc * TC_BN + half * 128);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tb + j * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sum[j * 32 + i] = __fadd_rn(sum[j * 32 + i], __uint_as_float(r[i]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty_leader0 + 8u * acc);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok) break;
+      const int row0 = m0 + quarter * 32;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col0 = n0 + half * 128 + j * 32;
+        float bias_lane = 0.0f;
+        if (add_bias && col0 + lane < p.n) bias_lane = __ldg(p.bias + col0 + lane);
+        float* v = sum + j * 32;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = v[i];
+          if (add_bias) x = __fadd_rn(x, __shfl_sync(0xffffffffu, bias_lane, i));
+          if (relu) x = (x != x) ? x : (x > 0.0f ? x : 0.0f);
+          v[i] = x;
+        }
+        if (row0 >= p.m || col0 >= p.n) continue;
+        if ((p.n & 3) && col0 + 32 > p.n) {
+          const int row = row0 + lane;
+          if (row < p.m) {
+            float* dst = p.c + (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.n) dst[i] = v[i];
+          }
+          continue;
+        }
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 w4 = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) = w4;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_3d(&tmC, buf, col0, row0, bt);
+          bulk_commit_group();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  } else {
+    reg_dealloc<Cfg::kOtherRegs>();
+    if (warp == TC_PRODUCER_WARP) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0) {
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued_parity[S];
+        for (int s = 0; s < S; ++s) issued_parity[s] = -1;
+        bool ok = true;
+        for (int t = pair; ok && t < p.tiles_total; t += npairs) {
+          int mt, nt, bt;
+          tc_tile_coords(p, t, mt, nt, bt);
+          const int m0 = mt * 256 + static_cast<int>(rank) * 128;
+          const int nb = nt * TC_BN + static_cast<int>(rank) * 128;  // this CTA's half of B
+          const int ba = p.a_batched ? bt : 0, bb = p.b_batched ? bt : 0;
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, ctl, kDevTimeoutEmpty)) { ok = false; break; }
+            uint8_t* sa = ops + stage * Cfg::kStageBytes;
+            uint8_t* sb = sa + Cfg::kABytes;
+            const int k0 = kb * Cfg::kBK;
+            mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+            if (A_MN) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) tma_load_3d(sa + i * Cfg::kMnAtomBytes, &tmA, &full[stage], m0 + 32 * i, k0, ba);
+            } else {
+              tma_load_3d(sa, &tmA, &full[stage], k0, m0, ba);
+            }
+            if (B_MN) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) tma_load_3d(sb + j * Cfg::kMnAtomBytes, &tmB, &full[stage], nb + 32 * j, k0, bb);
+            } else {
+              tma_load_3d(sb, &tmB, &full[stage], k0, nb, bb);
+            }
+            issued_parity[stage] = static_cast<int>(phase);
+            if (++stage == S) { stage = 0; phase ^= 1u; }
+          }
+        }
+        for (int s = 0; s < S; ++s) {
+          if (issued_parity[s] >= 0) {
+            const uint32_t a = smem_u32(&full[s]);
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(a, static_cast<uint32_t>(issued_parity[s]))) {
+              if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
+            }
+          }
+        }
+      }
+    } else if (warp == TC_MMA_WARP) {
+      if (lane == 0 && rank == 0) {
+        // ----------------------------------------------- MMA issuer (pair)
+        constexpr uint32_t idesc = idesc_tf32(256, TC_BN, A_MN, B_MN);
+        constexpr uint32_t a_layout = A_MN ? 1u : 4u, b_layout = B_MN ? 1u : 4u;
+        constexpr uint32_t a_lbo = A_MN ? Cfg::kMnAtomBytes : 16u, a_sbo = 512u;
+        constexpr uint32_t b_lbo = B_MN ? Cfg::kMnAtomBytes : 16u, b_sbo = 512u;
+        constexpr uint32_t a_kstep = A_MN ? 1024u : 32u, b_kstep = B_MN ? 1024u : 32u;
+        const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), 1);
+        const uint32_t acc_full_peer0 = mapa_shared(smem_u32(&acc_full[0]), 1);
+        int stage = 0;
+        uint32_t phase = 0;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        bool ok = true;
+        bool issued_any = false;
+        for (int t = pair; ok && t < p.tiles_total; t += npairs) {
+          uint32_t d_tmem = 0;
+          for (int kb = 0; kb < p.k_blocks; ++kb) {
+            const int kc = kb % p.chunk_kb;
+            if (kc == 0) {
+              if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
+              tc_fence_after();
+              d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
+            }
+            if (!mbar_wait_cluster(&split_done[stage], phase, ctl, kDevTimeoutXform)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(ops + stage * Cfg::kStageBytes);
+            const uint32_t sb = sa + Cfg::kABytes;
+            const uint32_t sa_lo = smem_u32(lo_ops + stage * Cfg::kStageBytes);
+            const uint32_t sb_lo = sa_lo + Cfg::kABytes;
+#pragma unroll
+            for (int kk = 0; kk < Cfg::kBK / 8; ++kk) {
+              const uint64_t ad = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_layout);
+              const uint64_t bd = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_layout);
+              const uint64_t ad_lo = smem_desc(sa_lo + kk * a_kstep, a_lbo, a_sbo, a_layout);
+              const uint64_t bd_lo = smem_desc(sb_lo + kk * b_kstep, b_lbo, b_sbo, b_layout);
+              umma_tf32_2sm(d_tmem, ad_lo, bd, idesc, (kc | kk) != 0);
+              umma_tf32_2sm(d_tmem, ad, bd_lo, idesc, 1u);
+              umma_tf32_2sm(d_tmem, ad, bd, idesc, 1u);
+            }
+            issued_any = true;
+            umma_commit_2sm(smem_u32(&empty[stage]));
+            umma_commit_2sm(empty_peer0 + 8u * stage);
+            if (++stage == S) { stage = 0; phase ^= 1u; }
+            if (kc == p.chunk_kb - 1 || kb == p.k_blocks - 1) {
+              umma_commit_2sm(smem_u32(&acc_full[acc]));
+              umma_commit_2sm(acc_full_peer0 + 8u * acc);
+              if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+            }
+          }
+        }
+        if (issued_any) {
+          umma_commit_2sm(smem_u32(drain));
+          umma_commit_2sm(mapa_shared(smem_u32(drain), 1));
+        }
+        if (issued_any) {
+          const uint32_t a = smem_u32(drain);
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait_cluster(a, 0u)) {
+            if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
+          }
+        }
+      }
+    } else if (warp >= TC_SPLIT_WARP0 && warp < TC_SPLIT_WARP0 + TC_SPLIT_WARPS) {
+      // ------------------------------------------------------- split warps
+      const int tid = threadIdx.x - TC_SPLIT_WARP0 * 32;
+      const uint32_t split_done_leader0 = mapa_shared(smem_u32(&split_done[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.tiles_total; t += npairs) {
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, ctl, kDevTimeoutFull)) { ok = false; break; }
+          const uint4* x = reinterpret_cast<const uint4*>(ops + stage * Cfg::kStageBytes);
+          uint4* lo = reinterpret_cast<uint4*>(lo_ops + stage * Cfg::kStageBytes);
+          bool nonfinite = false;
+#pragma unroll 4
+          for (int i = tid; i < Cfg::kStageBytes / 16; i += TC_SPLIT_WARPS * 32) {
+            const uint4 v = x[i];
+            uint4 l;
+#define MMR_SPLIT1(F)                                                                        \
+  {                                                                                          \
+    const uint32_t u = v.F;                                                                  \
+    const bool nf = (u & 0x7F800000u) == 0x7F800000u;                                        \
+    nonfinite |= nf;                                                                         \
+    l.F = nf ? 0u : __float_as_uint(__fsub_rn(__uint_as_float(u), __uint_as_float(u & 0xFFFFE000u))); \
+  }
+            MMR_SPLIT1(x) MMR_SPLIT1(y) MMR_SPLIT1(z) MMR_SPLIT1(w)
+#undef MMR_SPLIT1
+            lo[i] = l;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(split_done_leader0 + 8u * stage);
+          if (__any_sync(0xffffffffu, nonfinite) && lane == 0 && p.nf != nullptr) {
+            if (atomicOr(&p.nf[2 + t], 1u) == 0u) p.nf[2 + p.tiles_total + atomicAdd(&p.nf[0], 1u)] = t;
+          }
+          if (++stage == S) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  // On the normal path the epilogue consumed the last chunk's commit, which
+  // covers every MMA of the pair. After an error the odd CTA waits (bounded)
+  // for the drain commit before its TMEM and shared memory may go.
+  if (warp == TC_MMA_WARP && lane == 0 && rank == 1 && pair < p.tiles_total &&
+      *reinterpret_cast<volatile int*>(p.err) != 0) {
+    const uint32_t a = smem_u32(drain);
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait_cluster(a, 0u)) {
+      if (globaltimer_ns() - t0 > p.timeout_ns) break;
+    }
+  }
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its pair may still touch its memory
+  if (warp == TC_MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc_2sm(tmem_base, 512);
+  }
+}
+
+}  // namespace mmr
