@@ -243,7 +243,7 @@ def main():
     g = BoundGemm(node, A, B, C, BIAS, stream=stream.cuda_stream)
     gathered = None
     if world > 1:
-        gathered = torch.empty((world, n, out_t.shape[1]), dtype=torch.float32, device=dev)
+        gathered = torch.empty((world * n, out_t.shape[1]), dtype=torch.float32, device=dev)
 
     def step():
         g.replay()
