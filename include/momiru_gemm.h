@@ -208,7 +208,45 @@ MMR_API int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc *desc, int32_t *statu
  * `nranks` ranks in whole units of `align` columns (the output-tile width).
  * Pure host arithmetic. */
 MMR_API int32_t mmr_shard_columns(int64_t n, int32_t nranks, int32_t rank, int32_t align,
-                          int64_t *col0, int64_t *col1);
+                                  int64_t *col0, int64_t *col1);
+
+/* ---- device memory shared between the processes of one node ----------------
+ * One process drives one GPU; a rank maps its peers' buffers through CUDA IPC.
+ * `offset` is the address's distance from the start of its allocation, so
+ * buffers handed out by a caching allocator can be shared. */
+typedef struct mmr_ipc_handle {
+  uint8_t bytes[64];          /* cudaIpcMemHandle_t of the allocation         */
+  uint64_t offset;            /* address - allocation base                    */
+} mmr_ipc_handle;
+
+MMR_API int32_t mmr_ipc_export(uint64_t address, mmr_ipc_handle *out);
+/* Maps a peer's buffer into this process (on `device_ordinal`, which must be
+ * current-capable of peer access to the exporter). */
+MMR_API int32_t mmr_ipc_import(const mmr_ipc_handle *h, int32_t device_ordinal, uint64_t *address_out);
+MMR_API int32_t mmr_ipc_release(uint64_t address, const mmr_ipc_handle *h);
+
+/* ---- column-block sharded GEMM with the output replicated on every rank ----
+ * Rank r of `nranks` computes out[:, c0:c1] = epilogue(lhs @ rhs[:, c0:c1])
+ * for its column block (mmr_shard_columns, 256-column units) and every
+ * finished output tile is stored, by the GEMM's own epilogue, into the
+ * output replica of every rank over NVLink (peer stores). This is the
+ * all-gather of the reference IR's CollectiveKind::AllGather
+ * (src/momiru/tensor_light/execution/ir.rs:1140-1154), which the reference
+ * IR rejects today (ir.rs:1773-1779), fused into the GEMM. After the GEMM a
+ * one-block kernel publishes this rank's completion into every peer's signal
+ * array and waits (bounded; MMR_ERR_TIMEOUT via quiesce) until every peer
+ * has published, so a completed run means every replica is whole.
+ * `local` describes the full lhs, rhs, bias and this rank's full output
+ * replica; all ranks use the same shapes and the same output layout. */
+typedef struct mmr_sharded_desc {
+  mmr_matmul_desc local;
+  int32_t rank, nranks;       /* nranks <= 8                                  */
+  uint64_t peer_out[8];       /* rank i's output replica, mapped here         */
+  uint64_t peer_signal[8];    /* rank i's signal array (nranks u64), mapped   */
+  uint64_t signal;            /* this rank's signal array (zero-initialised)  */
+} mmr_sharded_desc;
+
+MMR_API int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc *desc, mmr_gemm_handle **out);
 
 #ifdef __cplusplus
 }

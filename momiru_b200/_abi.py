@@ -35,6 +35,7 @@ EXPORTED = [
     "mmr_gemm_validate", "mmr_gemm_bind", "mmr_gemm_run", "mmr_gemm_run_on", "mmr_gemm_quiesce",
     "mmr_gemm_destroy", "mmr_gemm_query", "mmr_last_error", "mmr_version",
     "mmr_selftest_bounded_wait", "mmr_shard_columns", "mmr_gemm_run_noalloc",
+    "mmr_ipc_export", "mmr_ipc_import", "mmr_ipc_release", "mmr_sharded_gemm_bind",
 ]
 NOALLOC_SCRATCH_BYTES = 64 * 1024
 NOALLOC_MAX_TILES = 8189
@@ -96,6 +97,21 @@ class MmrGemmInfo(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class MmrIpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_uint8 * 64), ("offset", ctypes.c_uint64)]
+
+
+class MmrShardedDesc(ctypes.Structure):
+    _fields_ = [
+        ("local", MmrMatmulDesc),
+        ("rank", ctypes.c_int32),
+        ("nranks", ctypes.c_int32),
+        ("peer_out", ctypes.c_uint64 * 8),
+        ("peer_signal", ctypes.c_uint64 * 8),
+        ("signal", ctypes.c_uint64),
+    ]
+
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libmomiru_gemm.so")
 _lib = None
@@ -123,6 +139,10 @@ def load() -> ctypes.CDLL:
     lib.mmr_version.restype = ctypes.c_char_p
     lib.mmr_selftest_bounded_wait.argtypes = [ctypes.c_int32, ctypes.c_uint64]
     lib.mmr_gemm_run_noalloc.argtypes = [P(MmrMatmulDesc), P(ctypes.c_int32)]
+    lib.mmr_ipc_export.argtypes = [ctypes.c_uint64, P(MmrIpcHandle)]
+    lib.mmr_ipc_import.argtypes = [P(MmrIpcHandle), ctypes.c_int32, P(ctypes.c_uint64)]
+    lib.mmr_ipc_release.argtypes = [ctypes.c_uint64, P(MmrIpcHandle)]
+    lib.mmr_sharded_gemm_bind.argtypes = [P(MmrShardedDesc), P(h)]
     lib.mmr_shard_columns.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       P(ctypes.c_int64), P(ctypes.c_int64)]
     for name in EXPORTED:

@@ -10,7 +10,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libmomiru_gemm.so")
 SOURCES = ["momiru_gemm.cu"]
-HEADERS = ["ptx.cuh", "tc_gemm.cuh", "simt_gemm.cuh", "gemv.cuh"]
+HEADERS = ["ptx.cuh", "tc_gemm.cuh", "tc_gemm_2sm.cuh", "simt_gemm.cuh", "gemv.cuh"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
@@ -40,7 +40,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         return LIB_PATH
     os.makedirs(LIB_DIR, exist_ok=True)
     cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-shared", "-o", LIB_PATH,
-           *[os.path.join(CSRC, s) for s in SOURCES], "-lcuda"]
+           *[os.path.join(CSRC, s) for s in SOURCES]]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)

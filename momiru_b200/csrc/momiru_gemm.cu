@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdint>
 #include <chrono>
 #include <cstdarg>
 #include <cstdio>
@@ -420,6 +421,12 @@ struct mmr_gemm_handle {
   int* h_err = nullptr;  // pinned host copy of the error word
   unsigned int* d_nf = nullptr;  // 3xTF32 non-finite bookkeeping
   int sms = 148;
+  // column-sharded GEMM with replicated output
+  bool sharded = false;
+  int rank = 0, nranks = 1;
+  unsigned long long* peer_signal[8] = {};
+  unsigned long long* signal = nullptr;
+  unsigned long long epoch = 0;
   cudaEvent_t done = nullptr, err_ev = nullptr;
   bool ran = false;
   uint64_t wait_timeout_ns = 2000000000ull;
@@ -906,6 +913,43 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
   return MMR_OK;
 }
 
+namespace {
+struct SignalParams {
+  unsigned long long* peer_signal[8];  // rank i's signal array (mapped here)
+  unsigned long long* local;           // this rank's signal array
+  int rank, nranks;
+  unsigned long long epoch;
+  int* err;
+  unsigned long long timeout_ns;
+};
+
+// After this rank's GEMM (whose epilogue fenced its peer stores system-wide):
+// publish `epoch` into every peer's slot for this rank, then wait, bounded,
+// until every peer has published into this rank's array. One warp.
+__global__ void replica_signal_wait_kernel(const SignalParams s) {
+  const int t = threadIdx.x;
+  const bool peer = t < s.nranks && t != s.rank;
+  if (peer) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(s.peer_signal[t] + s.rank), "l"(s.epoch) : "memory");
+  }
+  __syncwarp();
+  if (peer) {
+    const uint64_t t0 = mmr::globaltimer_ns();
+    for (;;) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(s.local + t) : "memory");
+      if (v >= s.epoch) break;
+      if (mmr::globaltimer_ns() - t0 > s.timeout_ns) {
+        atomicCAS(s.err, 0, mmr::kDevTimeoutPeer);
+        break;
+      }
+      __nanosleep(200);
+    }
+  }
+}
+}  // namespace
+
 int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
   if (!h) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -928,6 +972,18 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
         break;
       default: return fail(MMR_ERR_UNSUPPORTED_FAMILY, "no kernel bound");
     }
+  }
+  if (e == cudaSuccess && h->sharded) {
+    SignalParams sp{};
+    for (int i = 0; i < 8; ++i) sp.peer_signal[i] = h->peer_signal[i];
+    sp.local = h->signal;
+    sp.rank = h->rank;
+    sp.nranks = h->nranks;
+    sp.epoch = ++h->epoch;
+    sp.err = h->d_err;
+    sp.timeout_ns = h->wait_timeout_ns;
+    replica_signal_wait_kernel<<<1, 32, 0, s>>>(sp);
+    e = cudaGetLastError();
   }
   if (e != cudaSuccess) return fail(MMR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   MMR_CUDA_TRY(cudaEventRecord(h->done, s));
@@ -968,8 +1024,9 @@ int32_t mmr_gemm_quiesce(mmr_gemm_handle* h, uint64_t timeout_ns) {
   if (code != 0) {
     *h->h_err = 0;
     cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
-    return fail(code == mmr::kDevTimeoutDrain || code <= mmr::kDevTimeoutXform ? MMR_ERR_TIMEOUT
-                                                                               : MMR_ERR_DEVICE_FAULT_FLAG,
+    return fail(code == mmr::kDevTimeoutDrain || code <= mmr::kDevTimeoutXform || code == mmr::kDevTimeoutPeer
+                    ? MMR_ERR_TIMEOUT
+                    : MMR_ERR_DEVICE_FAULT_FLAG,
                 "kernel reported device error word %d (a bounded wait expired)", code);
   }
   return MMR_OK;
@@ -1140,6 +1197,119 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   if (ce != cudaSuccess) return fail(MMR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(ce));
   if (status_out)
     MMR_CUDA_TRY(cudaMemcpyAsync(status_out, dev->scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+  return MMR_OK;
+}
+
+int32_t mmr_ipc_export(uint64_t address, mmr_ipc_handle* out) {
+  if (!address || !out) return fail(MMR_ERR_INVALID_ARGUMENT, "null address or handle");
+  cudaPointerAttributes pa;
+  if (cudaPointerGetAttributes(&pa, reinterpret_cast<void*>(address)) != cudaSuccess ||
+      pa.type != cudaMemoryTypeDevice) {
+    cudaGetLastError();
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "address 0x%llx is not device memory", (unsigned long long)address);
+  }
+  DeviceGuard guard(pa.device);
+  // Driver entry point resolved through the runtime, so the library does not
+  // link libcuda directly (it must load on hosts without a driver).
+  typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static AddressRangeFn range_fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      range_fn = reinterpret_cast<AddressRangeFn>(ptr);
+  });
+  if (!range_fn) return fail(MMR_ERR_CUDA, "cuMemGetAddressRange is unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range_fn(&base, &size, static_cast<CUdeviceptr>(address)) != CUDA_SUCCESS)
+    return fail(MMR_ERR_CUDA, "cuMemGetAddressRange failed for 0x%llx", (unsigned long long)address);
+  cudaIpcMemHandle_t ih;
+  MMR_CUDA_TRY(cudaIpcGetMemHandle(&ih, reinterpret_cast<void*>(base)));
+  static_assert(sizeof(ih) == sizeof(out->bytes), "IPC handle size");
+  memcpy(out->bytes, &ih, sizeof ih);
+  out->offset = address - static_cast<uint64_t>(base);
+  return MMR_OK;
+}
+
+int32_t mmr_ipc_import(const mmr_ipc_handle* h, int32_t device_ordinal, uint64_t* address_out) {
+  if (!h || !address_out) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle or output");
+  DeviceGuard guard(device_ordinal);
+  if (!guard.ok) return fail(MMR_ERR_CUDA, "cudaSetDevice(%d) failed", device_ordinal);
+  cudaIpcMemHandle_t ih;
+  memcpy(&ih, h->bytes, sizeof ih);
+  void* p = nullptr;
+  MMR_CUDA_TRY(cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess));
+  *address_out = reinterpret_cast<uint64_t>(p) + h->offset;
+  return MMR_OK;
+}
+
+int32_t mmr_ipc_release(uint64_t address, const mmr_ipc_handle* h) {
+  if (!address || !h) return fail(MMR_ERR_INVALID_ARGUMENT, "null address or handle");
+  MMR_CUDA_TRY(cudaIpcCloseMemHandle(reinterpret_cast<void*>(address - h->offset)));
+  return MMR_OK;
+}
+
+int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc* d, mmr_gemm_handle** out) {
+  if (!d || !out) return fail(MMR_ERR_INVALID_ARGUMENT, "null descriptor or output handle");
+  *out = nullptr;
+  if (d->nranks < 1 || d->nranks > 8 || d->rank < 0 || d->rank >= d->nranks)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "rank %d of %d outside 1..8 ranks", d->rank, d->nranks);
+  if (!d->signal) return fail(MMR_ERR_INVALID_ARGUMENT, "null signal array");
+  for (int i = 0; i < d->nranks; ++i)
+    if (i != d->rank && (!d->peer_out[i] || !d->peer_signal[i]))
+      return fail(MMR_ERR_INVALID_ARGUMENT, "rank %d's replica or signal array is not mapped", i);
+  // Validate the whole node first, then narrow to this rank's column block.
+  Plan whole;
+  int32_t rc = build_plan(&d->local, &whole);
+  if (rc) return rc;
+  const mmr_view& O = d->local.out;
+  if (O.rank < 2 || d->local.rhs.rank < 2)
+    return fail(MMR_ERR_INVALID_SHAPE, "column sharding needs matrix operands (rank >= 2)");
+  int64_t c0 = 0, c1 = 0;
+  if ((rc = mmr_shard_columns(whole.n, d->nranks, d->rank, mmr::TC_BN, &c0, &c1))) return rc;
+  mmr_matmul_desc local = d->local;
+  local.family = MMR_FAMILY_TCGEN05;
+  // out[..., c0:c1]
+  local.out.base_offset_bytes += uint64_t(c0) * uint64_t(O.strides[O.rank - 1]) * 4u;
+  local.out.dims[O.rank - 1] = c1 - c0;
+  // rhs[..., :, c0:c1] (columns are the rhs's last axis, or its second to last when transposed)
+  const mmr_view& R = d->local.rhs;
+  const int raxis = d->local.transpose_rhs ? R.rank - 2 : R.rank - 1;
+  local.rhs.base_offset_bytes += uint64_t(c0) * uint64_t(R.strides[raxis]) * 4u;
+  local.rhs.dims[raxis] = c1 - c0;
+  if (local.epilogue == MMR_EPI_BIAS || local.epilogue == MMR_EPI_BIAS_RELU) {
+    local.bias.base_offset_bytes += uint64_t(c0) * uint64_t(local.bias.strides[0]) * 4u;
+    local.bias.dims[0] = c1 - c0;
+  }
+  mmr_gemm_handle* h = nullptr;
+  if (c1 > c0) {
+    if ((rc = mmr_gemm_bind(&local, &h))) return rc;
+  } else {
+    // An empty column block still takes part in the completion handshake.
+    local.family = MMR_FAMILY_AUTO;
+    if ((rc = mmr_gemm_bind(&local, &h))) return rc;
+  }
+  h->sharded = true;
+  h->rank = d->rank;
+  h->nranks = d->nranks;
+  h->signal = reinterpret_cast<unsigned long long*>(d->signal);
+  const uint64_t view_off = local.out.address + local.out.base_offset_bytes - O.address;
+  int q = 0;
+  for (int i = 0; i < d->nranks; ++i) {
+    h->peer_signal[i] = reinterpret_cast<unsigned long long*>(d->peer_signal[i]);
+    if (i == d->rank) continue;
+    float* pc = reinterpret_cast<float*>(d->peer_out[i] + view_off);
+    h->tcp.peer_c[q] = pc;
+    h->sp.peer_c[q] = pc;
+    ++q;
+  }
+  h->tcp.npeers = q;
+  h->sp.npeers = q;
+  *out = h;
   return MMR_OK;
 }
 

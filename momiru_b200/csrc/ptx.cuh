@@ -16,7 +16,8 @@ enum : int {
   kDevTimeoutAcc = 3,    // MMA or epilogue gave up on the TMEM accumulator
   kDevTimeoutXform = 4,  // MMA gave up waiting for the split operands
   kDevTimeoutDrain = 5,  // teardown gave up draining in-flight copies
-  kDevTimeoutProbe = 6   // the bounded-wait self test expired (expected)
+  kDevTimeoutProbe = 6,  // the bounded-wait self test expired (expected)
+  kDevTimeoutPeer = 7    // a peer rank never published its replica stores
 };
 
 struct WaitCtl {

@@ -21,6 +21,10 @@ struct SimtParams {
   float* c; long long c_b0, c_b1, c_m, c_n;
   const float* bias; long long bias_n;
   int epilogue;  // 0 none, 1 bias, 2 bias+relu, 3 relu
+  // Replicas of C on other ranks (same element offsets), for the exact
+  // recompute of a column-sharded GEMM's flagged tiles.
+  int npeers;
+  float* peer_c[7];
 };
 
 constexpr int SIMT_BM = 64, SIMT_BN = 64, SIMT_BK = 16;
@@ -82,6 +86,8 @@ __device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, in
       if (add_bias) x = __fadd_rn(x, p.bias[gn * p.bias_n]);
       if (relu) x = (x != x) ? x : (x > 0.0f ? x : 0.0f);
       C[gm * p.c_m + gn * p.c_n] = x;
+      for (int q = 0; q < p.npeers; ++q)
+        p.peer_c[q][b0 * p.c_b0 + b1 * p.c_b1 + gm * p.c_m + gn * p.c_n] = x;
     }
   }
 }

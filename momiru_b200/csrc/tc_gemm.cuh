@@ -46,6 +46,7 @@ constexpr int TC_MMA_WARP = 9;
 constexpr int TC_SPLIT_WARP0 = 10;
 constexpr int TC_SPLIT_WARPS = 6;
 constexpr int TC_GROUP_M = 16;                  // tile raster: M-tiles per group
+constexpr int kMaxPeers = 7;                    // replicas on other ranks (8 GPUs)
 
 enum : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU = 3 };
 
@@ -105,7 +106,29 @@ struct TcParams {
   // Non-finite bookkeeping (3xTF32): [0] count, [1] blocks done,
   // [2, 2+tiles) per-tile flags, [2+tiles, 2+2*tiles) flagged tile list.
   unsigned int* nf;
+  // Replicated output (column-sharded GEMM): every finished box is also
+  // stored into each peer rank's copy of C, at the same element offsets from
+  // peer_c[i] as from c (addresses mapped into this process).
+  int npeers;
+  float* peer_c[kMaxPeers];
 };
+
+// Copies one finished 32x32 box from the 128B-swizzled staging buffer to each
+// peer replica: per instruction the warp writes four 128-byte row segments.
+// Called by a whole warp after the staging writes and a __syncwarp.
+__device__ __forceinline__ void store_box_to_peers(const TcParams& p, const uint8_t* buf, int row0, int col0,
+                                                   int bt, int lane) {
+#pragma unroll 1
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    const int ch = lane & 7;
+    const float4 v = *reinterpret_cast<const float4*>(buf + r * 128 + ((ch ^ (r & 7)) << 4));
+    if (row0 + r < p.m && col0 + ch * 4 < p.n) {
+      const long long off = (long long)bt * p.c_bs + (long long)(row0 + r) * p.c_ld + col0 + ch * 4;
+      for (int q = 0; q < p.npeers; ++q) *reinterpret_cast<float4*>(p.peer_c[q] + off) = v;
+    }
+  }
+}
 
 __device__ __forceinline__ void tc_tile_coords(const TcParams& p, int t, int& mt, int& nt, int& bt) {
   const int per_batch = p.tiles_m * p.tiles_n;
@@ -236,10 +259,13 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
           // valid columns one by one instead.
           const int row = row0 + lane;
           if (row < p.m) {
-            float* dst = p.c + (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
+            const long long off = (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (col0 + i < p.n) dst[i] = v[i];
+              if (col0 + i < p.n) p.c[off + i] = v[i];
+            for (int q = 0; q < p.npeers; ++q)
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < p.n) p.peer_c[q][off + i] = v[i];
           }
           continue;
         }
@@ -257,9 +283,11 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
           tma_store_3d(&tmC, buf, col0, row0, bt);
           bulk_commit_group();
         }
+        if (p.npeers) store_box_to_peers(p, buf, row0, col0, bt, lane);
       }
     }
     if (lane == 0) bulk_wait_group_all();
+    if (p.npeers) __threadfence_system();  // peer stores ordered before the completion signal
     __syncwarp();
   } else {
     reg_dealloc<Cfg::kOtherRegs>();
@@ -447,6 +475,7 @@ __global__ void __launch_bounds__(256) tc_nonfinite_fixup_kernel(const SimtParam
     const int n0 = nt * TC_BN + (sub % (TC_BN / SIMT_BN)) * SIMT_BN;
     simt_block_exact(sp, m0, n0, bt, As, Bs);
   }
+  if (sp.npeers) __threadfence_system();
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) last = (atomicAdd(&p.nf[1], 1u) == gridDim.x - 1);

@@ -153,10 +153,13 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
         if ((p.n & 3) && col0 + 32 > p.n) {
           const int row = row0 + lane;
           if (row < p.m) {
-            float* dst = p.c + (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
+            const long long off = (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (col0 + i < p.n) dst[i] = v[i];
+              if (col0 + i < p.n) p.c[off + i] = v[i];
+            for (int q = 0; q < p.npeers; ++q)
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < p.n) p.peer_c[q][off + i] = v[i];
           }
           continue;
         }
@@ -173,9 +176,11 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
           tma_store_3d(&tmC, buf, col0, row0, bt);
           bulk_commit_group();
         }
+        if (p.npeers) store_box_to_peers(p, buf, row0, col0, bt, lane);
       }
     }
     if (lane == 0) bulk_wait_group_all();
+    if (p.npeers) __threadfence_system();  // peer stores ordered before the completion signal
     __syncwarp();
   } else {
     reg_dealloc<Cfg::kOtherRegs>();

@@ -75,3 +75,92 @@ class GatherLayout:
         for r, (c0, c1) in enumerate(self.shards):
             out[:, c0:c1] = gathered[r][:, :c1 - c0]
         return out
+
+
+class ReplicatedColumnGemm:
+    """Column-sharded GEMM whose output is replicated on every rank.
+
+    One process per GPU, `torch.distributed` initialised (any backend: it only
+    carries the 72-byte IPC handles at bind time). Each rank passes the full
+    lhs, rhs, bias views and a full output replica of its own; the node is
+    bound with mmr_sharded_gemm_bind, whose GEMM epilogue stores every finished
+    output tile into all replicas over NVLink, followed by a bounded
+    completion handshake. No collective runs on the data path.
+    """
+
+    def __init__(self, node, lhs, rhs, out, bias=None, stream=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _abi, execution
+        self._lib = _abi.load()
+        self.rank = dist.get_rank()
+        self.world = dist.get_world_size()
+        if self.world > 8:
+            raise execution.InvalidArgument("at most 8 ranks", _abi.ERR_INVALID_ARGUMENT)
+        dev = out.buffer.device_ordinal
+        self._views = (lhs, rhs, out, bias)
+        self._signal = torch.zeros(8, dtype=torch.int64, device=f"cuda:{dev}")
+        torch.cuda.synchronize(dev)
+
+        def export(addr):
+            h = _abi.MmrIpcHandle()
+            execution._check(self._lib.mmr_ipc_export(addr, ctypes.byref(h)))
+            return bytes(h.bytes), int(h.offset)
+
+        mine = (export(out.buffer.address), export(self._signal.data_ptr()))
+        everyone = [None] * self.world
+        dist.all_gather_object(everyone, mine)
+        self._imported = []
+        d = _abi.MmrShardedDesc()
+        d.local = execution._desc(node, lhs, rhs, out, bias, stream)
+        d.rank = self.rank
+        d.nranks = self.world
+        d.signal = self._signal.data_ptr()
+        for r, ((ob, oo), (sb, so)) in enumerate(everyone):
+            if r == self.rank:
+                d.peer_out[r] = out.buffer.address
+                d.peer_signal[r] = self._signal.data_ptr()
+                continue
+            for i, (b, off) in enumerate(((ob, oo), (sb, so))):
+                h = _abi.MmrIpcHandle()
+                ctypes.memmove(h.bytes, b, 64)
+                h.offset = off
+                addr = ctypes.c_uint64()
+                execution._check(self._lib.mmr_ipc_import(ctypes.byref(h), dev, ctypes.byref(addr)))
+                self._imported.append((addr.value, h))
+                if i == 0:
+                    d.peer_out[r] = addr.value
+                else:
+                    d.peer_signal[r] = addr.value
+        self._handle = ctypes.c_void_p()
+        execution._check(self._lib.mmr_sharded_gemm_bind(ctypes.byref(d), ctypes.byref(self._handle)))
+        info = _abi.MmrGemmInfo()
+        execution._check(self._lib.mmr_gemm_query(self._handle, ctypes.byref(info)))
+        self.info = info.as_dict()
+        self.columns = column_shards(out.dims[-1], self.world)[self.rank]
+
+    def replay(self):
+        from . import execution
+        execution._check(self._lib.mmr_gemm_run(self._handle))
+
+    def quiesce_or_abort(self, timeout_s: float = 60.0):
+        from . import execution
+        execution._check(self._lib.mmr_gemm_quiesce(self._handle, int(timeout_s * 1e9)))
+
+    def close(self):
+        import ctypes
+        if self._handle:
+            self._lib.mmr_gemm_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+        for addr, h in self._imported:
+            self._lib.mmr_ipc_release(addr, ctypes.byref(h))
+        self._imported = []
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
