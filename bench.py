@@ -55,6 +55,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--workload", choices=["c3", "c1", "c2", "c4", "c5a", "c5b"], default="c3",
+                    help="c3 (default) is the headline line; the others are the remaining configurations, "
+                         "measured the same way and reported one JSON line each")
     return ap.parse_args()
 
 
@@ -205,11 +208,138 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_workload(args, rank, world, local):
+    """The non-headline configurations, device-timed with CUDA events.
+
+    c1  512^3 row-major                        (TFLOP/s, tensor roofline)
+    c2  [64,256,256] @ [256,256] broadcast     (TFLOP/s)
+    c4  A = X^T view, B = W[:, :11008] view    (TFLOP/s)
+    c5a [512,1024,1024] @ [512,1024,1024]      (TFLOP/s; batch-sharded over ranks, no collective)
+    c5b [M,4096] @ [4096,4096], M in 1,4,16    (HBM GB/s; four B copies rotate so L2 cannot serve them)
+    """
+    import torch
+    import torch.distributed as dist
+    from momiru_b200 import (AccuracyContract, BoundGemm, DeviceBuffer, DeviceView, Epilogue, KernelMathMode,
+                             MatMulNode, rng)
+    from momiru_b200.sharding import batch_shards
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    dev = local
+    mode = KernelMathMode.StrictFp32 if args.mode == "strict" else KernelMathMode.Tf32
+    acc = AccuracyContract.StrictFp32 if args.mode == "strict" else AccuracyContract.AllowTf32
+    node = MatMulNode(math_mode=mode, accuracy=acc)
+    stream = torch.cuda.current_stream()
+    peaks = load_peaks()
+    lines = []
+
+    def dv(arr):
+        return DeviceView.from_host(arr, dev)
+
+    def timed(handles, flops, bytes_, name, cfg, bound):
+        for _ in range(max(args.warmup, 3)):
+            for h in handles:
+                h.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            handles[i % len(handles)].replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], device=f"cuda:{dev}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        for h in handles:
+            h.quiesce_or_abort(60)
+        tf32_peak = peaks["bf16_tflops"] / 2.0
+        if bound == "hbm":
+            value, unit, peak = bytes_ / (ms * 1e-3) / 1e9, "GB/s", peaks["hbm_gbs"]
+        else:
+            value, unit = flops / (ms * 1e-3) / 1e12, "TFLOP/s"
+            peak = tf32_peak / 3.0 if args.mode == "strict" else tf32_peak
+        per_rank = value / world
+        lines.append({
+            "metric": name, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak" if args.workload == "c5a" and world > 1 else "replicas" if world > 1 else "n/a",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64)", "config": cfg,
+            "math": "3xTF32 (StrictFp32)" if args.mode == "strict" else "TF32",
+            "family": handles[0].family,
+            "roofline": {"bound": bound, "achieved": per_rank, "peak": peak, "unit": unit, "frac": per_rank / peak,
+                         "peak_basis": "measured HBM copy" if bound == "hbm" else
+                         f"measured bf16 dense / 2{' / 3' if args.mode == 'strict' else ''}"},
+        })
+
+    w = args.workload
+    if w == "c1":
+        a, b = dv(rng.randu((512, 512), 1)), dv(rng.randu((512, 512), 2))
+        out = DeviceView.empty((512, 512), dev)
+        timed([BoundGemm(node, a, b, out, stream=stream.cuda_stream)], 2.0 * 512 ** 3, 3 * 4 * 512 ** 2,
+              "C1 512^3 f32 GEMM TFLOP/s", {"workload": "c1_512^3", "l2": "resident (small case)"}, "tensor")
+    elif w == "c2":
+        a, b = dv(rng.randn((64, 256, 256), 1)), dv(rng.randn((256, 256), 2))
+        out = DeviceView.empty((64, 256, 256), dev)
+        timed([BoundGemm(node, a, b, out, stream=stream.cuda_stream)], 2.0 * 64 * 256 ** 3,
+              4 * (2 * 64 * 256 * 256 + 256 * 256), "C2 batched 64x256^3 (B broadcast) TFLOP/s",
+              {"workload": "c2_batch64_256^3_bcast", "l2": "resident (33.8 MB)"}, "tensor")
+    elif w == "c4":
+        x, wt = dv(rng.randn((4096, 4096), 1, 0.02)), dv(rng.randn((4096, 12288), 2, 0.02))
+        out = DeviceView.empty((4096, 11008), dev)
+        timed([BoundGemm(node, x.transpose(), wt.narrow(1, 0, 11008), out, stream=stream.cuda_stream)],
+              2.0 * 4096 * 4096 * 11008, 4 * (4096 * 4096 + 2 * 4096 * 11008),
+              "C4 strided views 4096x4096x11008 TFLOP/s",
+              {"workload": "c4_xT_4096_wslice_11008", "l2": "inputs 245 MB > L2"}, "tensor")
+    elif w == "c5a":
+        b0, b1 = batch_shards(512, world)[rank]
+        nb = b1 - b0
+        a = DeviceView.empty((nb, 1024, 1024), dev)
+        b = DeviceView.empty((nb, 1024, 1024), dev)
+        # one seeded block of 16 batch entries, repeated over the rank's slice
+        # (the values do not change the throughput)
+        blk_a = torch.from_numpy(rng.randu((16, 1024, 1024), 1)).to(f"cuda:{dev}")
+        blk_b = torch.from_numpy(rng.randu((16, 1024, 1024), 2)).to(f"cuda:{dev}")
+        at, bt = a.torch_view(), b.torch_view()
+        for i in range(0, nb, 16):
+            j = min(16, nb - i)
+            at[i:i + j].copy_(blk_a[:j])
+            bt[i:i + j].copy_(blk_b[:j])
+        out = DeviceView.empty((nb, 1024, 1024), dev)
+        timed([BoundGemm(node, a, b, out, stream=stream.cuda_stream)], 2.0 * 512 * 1024 ** 3,
+              4 * 3 * 512 * 1024 ** 2, "C5a batched 512x1024^3 TFLOP/s",
+              {"workload": "c5a_batch512_1024^3", "parallelism": f"batch-shard x{world}, no collective",
+               "l2": "inputs 4 GiB > L2"}, "tensor")
+    elif w == "c5b":
+        bs = [dv(rng.randn((4096, 4096), 10 + i)) for i in range(4)]
+        for m in (1, 4, 16):
+            a = dv(rng.randn((m, 4096), 1))
+            outs = [DeviceView.empty((m, 4096), dev) for _ in range(4)]
+            hs = [BoundGemm(MatMulNode(), a, bs[i], outs[i], stream=stream.cuda_stream) for i in range(4)]
+            timed(hs, 2.0 * m * 4096 * 4096, 4 * (m * 4096 + 4096 * 4096 + m * 4096),
+                  f"C5b GEMV M={m} N=K=4096 HBM GB/s",
+                  {"workload": f"c5b_gemv_m{m}", "l2": "four 64 MiB B copies rotate (256 MiB > L2)"}, "hbm")
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        for line in lines:
+            print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args)
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload != "c3":
+        run_workload(args, rank, world, local)
         return
     import torch
     import torch.distributed as dist
