@@ -1,139 +1,217 @@
 // gemv.cuh -- skinny-M (M <= 16) f32 matmul that streams B from HBM once.
 //
-// y[m, n] = epilogue(sum_k A[m, k] * B[k, n]) for a row-major (N-contiguous)
-// B. The work is HBM-bound (B is read exactly once, 4*K*N bytes), so the
-// kernel is judged in GB/s, not FLOP/s. Layout of the launch:
-//   grid.x  = ceil(N / 128) column blocks of 128 columns (32 lanes x float4)
-//   grid.y  = GV_KSPLIT K-slices, one thread-block cluster of GV_KSPLIT CTAs
-//             per column block (cluster dims 1 x GV_KSPLIT x 1)
-//   8 warps per CTA split the CTA's K-slice again.
-// Partial sums are reduced in a fixed order -- warps through shared memory,
-// then the cluster's CTAs through distributed shared memory -- so results are
-// deterministic run to run, without atomics or a global scratch buffer.
+// y[m, n] = epilogue(sum_k A[m, k] * B[k, n]) for a row-major B. The work is
+// HBM-bound (B is read exactly once, 4*K*N bytes), so the kernel is judged in
+// GB/s. Launch:
+//   grid.x  = ceil(N / 128) column strips of 128 columns
+//   grid.y  = GV_KSPLIT K-slices; the GV_KSPLIT CTAs of a strip form one
+//             thread-block cluster (dims 1 x GV_KSPLIT x 1)
+//   block   = 8 consumer warps + 1 producer warp
+// The producer thread streams the CTA's B slice through a GV_STAGES-deep
+// shared-memory ring with TMA (32 rows x 128 columns, 16 KiB per stage), so
+// the bytes in flight do not depend on registers; the consumer warps take 4
+// rows of each stage (lane = 4 columns) and accumulate M x 4 partial sums.
+// Partials are reduced in a fixed order -- warps through shared memory (the
+// idle ring), then the cluster's CTAs through distributed shared memory -- so
+// results are deterministic, without atomics or a global scratch buffer.
+// Waits are bounded like the GEMM's.
 #pragma once
 #include <cooperative_groups.h>
 #include <stdint.h>
 
+#include "ptx.cuh"
+
 namespace mmr {
 
-constexpr int GV_THREADS = 256;
-constexpr int GV_WARPS = GV_THREADS / 32;
+constexpr int GV_CONSUMER_WARPS = 8;
+constexpr int GV_THREADS = 32 * (GV_CONSUMER_WARPS + 1);
 constexpr int GV_COLS = 128;
+constexpr int GV_ROWS = 32;                             // B rows per stage
+constexpr int GV_STAGE_BYTES = GV_ROWS * GV_COLS * 4;   // 16 KiB
+constexpr int GV_STAGES = 4;
 constexpr int GV_KSPLIT = 8;
 constexpr int GV_MAX_M = 16;
 constexpr int GV_MAX_KSLICE = 1024;  // K <= GV_KSPLIT * GV_MAX_KSLICE = 8192
 
 struct GemvParams {
   int m, n, k;
-  int kslice;  // ceil(K / GV_KSPLIT), a multiple of GV_WARPS
+  int kslice;  // ceil(K / GV_KSPLIT) rounded up to GV_ROWS
   const float* a; long long a_m, a_k;
-  const float* b; long long b_k;  // B row stride (elements); column stride 1
   float* c; long long c_m;        // C row stride; column stride 1
   const float* bias;
   int epilogue;
+  int* err;
+  unsigned long long timeout_ns;
 };
 
-// Dynamic shared memory: A slice [MT][kslice], per-warp partials
-// [GV_WARPS][MT][128], and the CTA partial [MT][128] that cluster peers read.
+// Dynamic shared memory: the stage ring (reused afterwards for the per-warp
+// partials [8][MT][128]), the A slice [MT][kslice], the CTA partial [MT][128]
+// that cluster peers read, and the ring's barriers.
+__host__ __device__ constexpr int gemv_ring_bytes(int mt) {
+  return (GV_STAGES * GV_STAGE_BYTES > GV_CONSUMER_WARPS * mt * GV_COLS * 4)
+             ? GV_STAGES * GV_STAGE_BYTES
+             : GV_CONSUMER_WARPS * mt * GV_COLS * 4;
+}
 __host__ __device__ constexpr int gemv_smem_bytes(int mt, int kslice) {
-  return (mt * kslice + GV_WARPS * mt * GV_COLS + mt * GV_COLS) * 4;
+  return gemv_ring_bytes(mt) + mt * kslice * 4 + mt * GV_COLS * 4 + 2 * GV_STAGES * 8 + 1024;
 }
 
 template <int MT>
-__global__ void __launch_bounds__(GV_THREADS) gemv_cluster_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap tmB,
+                                                                  const GemvParams p) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ float4 gv_smem4[];
-  float* smem = reinterpret_cast<float*>(gv_smem4);
-  float* As = smem;                                   // [MT][kslice]
-  float* red = smem + MT * p.kslice;                  // [warp][MT][128]
-  float* part = red + GV_WARPS * MT * GV_COLS;        // [MT][128]
+  extern __shared__ uint8_t gv_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gv_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = base;                                                  // [GV_STAGES][32][128] f32
+  float* red = reinterpret_cast<float*>(base);                           // aliases the ring afterwards
+  float* As = reinterpret_cast<float*>(base + gemv_ring_bytes(MT));      // [MT][kslice]
+  float* part = As + MT * p.kslice;                                      // [MT][128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(part + MT * GV_COLS);
+  uint64_t* empty = full + GV_STAGES;
 
   const int rank = static_cast<int>(cluster.block_rank());  // K-slice index
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col0 = blockIdx.x * GV_COLS;
   const int k_lo = rank * p.kslice;
   const int k_hi = min(p.k, k_lo + p.kslice);
+  const int nstages = k_hi > k_lo ? (k_hi - k_lo + GV_ROWS - 1) / GV_ROWS : 0;
+  const WaitCtl ctl{p.err, p.timeout_ns};
 
-  for (int idx = threadIdx.x; idx < MT * p.kslice; idx += GV_THREADS) {
-    const int mm = idx / p.kslice, kk = idx - mm * p.kslice;
-    const int gk = k_lo + kk;
-    As[idx] = (mm < p.m && gk < k_hi) ? p.a[mm * p.a_m + gk * p.a_k] : 0.0f;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GV_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], GV_CONSUMER_WARPS);
+    }
+    fence_mbar_init();
   }
   __syncthreads();
+
+  if (warp == GV_CONSUMER_WARPS) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmB);
+      int issued = 0;
+      for (int s = 0; s < nstages; ++s) {
+        const int slot = s % GV_STAGES;
+        const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
+        if (!mbar_wait(&empty[slot], phase ^ 1u, ctl, kDevTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&full[slot], GV_STAGE_BYTES);
+        tma_load_3d(ring + slot * GV_STAGE_BYTES, &tmB, &full[slot], col0, k_lo + s * GV_ROWS, 0);
+        ++issued;
+      }
+      // Every issued load must land before the ring is reused or the CTA
+      // exits (already true on the normal path).
+      for (int s = issued > GV_STAGES ? issued - GV_STAGES : 0; s < issued; ++s) {
+        const uint32_t a = smem_u32(&full[s % GV_STAGES]);
+        const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(a, phase)) {
+          if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
+        }
+      }
+    }
+  } else {
+    // A slice into shared memory while the first stages are in flight; the
+    // loads are independent, so issue them back to back (16-byte vectors when
+    // A's rows are K-contiguous and aligned).
+    const bool vec = p.a_k == 1 && (p.a_m & 3) == 0 && (k_lo & 3) == 0 &&
+                     (reinterpret_cast<uintptr_t>(p.a) & 15u) == 0;
+    if (vec) {
+      const int q4 = p.kslice >> 2;  // kslice is a multiple of 32
+#pragma unroll 4
+      for (int idx = threadIdx.x; idx < MT * q4; idx += GV_CONSUMER_WARPS * 32) {
+        const int mm = idx / q4, kk = (idx - mm * q4) * 4;
+        const int gk = k_lo + kk;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (mm < p.m) {
+          if (gk + 3 < k_hi) {
+            v = __ldg(reinterpret_cast<const float4*>(p.a + mm * p.a_m + gk));
+          } else {
+            if (gk < k_hi) v.x = p.a[mm * p.a_m + gk];
+            if (gk + 1 < k_hi) v.y = p.a[mm * p.a_m + gk + 1];
+            if (gk + 2 < k_hi) v.z = p.a[mm * p.a_m + gk + 2];
+          }
+        }
+        *reinterpret_cast<float4*>(As + mm * p.kslice + kk) = v;
+      }
+    } else {
+#pragma unroll 8
+      for (int idx = threadIdx.x; idx < MT * p.kslice; idx += GV_CONSUMER_WARPS * 32) {
+        const int mm = idx / p.kslice, kk = idx - mm * p.kslice;
+        const int gk = k_lo + kk;
+        As[idx] = (mm < p.m && gk < k_hi) ? p.a[mm * p.a_m + gk * p.a_k] : 0.0f;
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(GV_CONSUMER_WARPS * 32) : "memory");  // consumers only
+  }
 
   float acc[MT][4];
 #pragma unroll
   for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
 
-  const int wk = p.kslice / GV_WARPS;  // rows per warp
-  const int wk_lo = k_lo + warp * wk;
-  const int wk_hi = min(k_hi, wk_lo + wk);
-  const int col = col0 + lane * 4;
-  if (col < p.n) {
-    const float* bcol = p.b + col;
-    int k = wk_lo;
-    for (; k + 8 <= wk_hi; k += 8) {
-      float4 bv[8];
+  if (warp < GV_CONSUMER_WARPS) {
+    // ---------------------------------------------------------- consumers
+    for (int s = 0; s < nstages; ++s) {
+      const int slot = s % GV_STAGES;
+      const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
+      if (!mbar_wait(&full[slot], phase, ctl, kDevTimeoutFull)) break;
+      const uint8_t* st = ring + slot * GV_STAGE_BYTES;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) bv[u] = __ldg(reinterpret_cast<const float4*>(bcol + (long long)(k + u) * p.b_k));
+      for (int r = 0; r < 4; ++r) {
+        const int row = warp * 4 + r;
+        const int k = k_lo + s * GV_ROWS + row;
+        if (k < k_hi) {
+          const float4 bv = *reinterpret_cast<const float4*>(st + row * (GV_COLS * 4) + lane * 16);
+          const float* arow = As + (k - k_lo);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float* arow = As + (k + u - k_lo);
-#pragma unroll
-        for (int i = 0; i < MT; ++i) {
-          const float av = arow[i * p.kslice];
-          acc[i][0] = fmaf(av, bv[u].x, acc[i][0]);
-          acc[i][1] = fmaf(av, bv[u].y, acc[i][1]);
-          acc[i][2] = fmaf(av, bv[u].z, acc[i][2]);
-          acc[i][3] = fmaf(av, bv[u].w, acc[i][3]);
+          for (int i = 0; i < MT; ++i) {
+            const float av = arow[i * p.kslice];
+            acc[i][0] = fmaf(av, bv.x, acc[i][0]);
+            acc[i][1] = fmaf(av, bv.y, acc[i][1]);
+            acc[i][2] = fmaf(av, bv.z, acc[i][2]);
+            acc[i][3] = fmaf(av, bv.w, acc[i][3]);
+          }
         }
       }
-    }
-    for (; k < wk_hi; ++k) {
-      const float4 bv = __ldg(reinterpret_cast<const float4*>(bcol + (long long)k * p.b_k));
-      const float* arow = As + (k - k_lo);
-#pragma unroll
-      for (int i = 0; i < MT; ++i) {
-        const float av = arow[i * p.kslice];
-        acc[i][0] = fmaf(av, bv.x, acc[i][0]);
-        acc[i][1] = fmaf(av, bv.y, acc[i][1]);
-        acc[i][2] = fmaf(av, bv.z, acc[i][2]);
-        acc[i][3] = fmaf(av, bv.w, acc[i][3]);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
     }
   }
-#pragma unroll
-  for (int i = 0; i < MT; ++i)
-    *reinterpret_cast<float4*>(red + (warp * MT + i) * GV_COLS + lane * 4) =
-        make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-  __syncthreads();
+  __syncthreads();  // the ring is idle from here on: reuse it for partials
 
+  if (warp < GV_CONSUMER_WARPS) {
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+      *reinterpret_cast<float4*>(red + (warp * MT + i) * GV_COLS + lane * 4) =
+          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+  }
+  __syncthreads();
   // CTA partial: fixed warp order 0..7.
   for (int idx = threadIdx.x; idx < MT * GV_COLS; idx += GV_THREADS) {
-    float s = 0.0f;
+    float sum = 0.0f;
 #pragma unroll
-    for (int w = 0; w < GV_WARPS; ++w) s += red[w * MT * GV_COLS + idx];
-    part[idx] = s;
+    for (int w = 0; w < GV_CONSUMER_WARPS; ++w) sum += red[w * MT * GV_COLS + idx];
+    part[idx] = sum;
   }
   cluster.sync();
 
   // Cluster reduction through DSMEM: CTA `rank` finalises a 1/GV_KSPLIT slice
-  // of this column block's MT x 128 outputs, summing ranks 0..7 in order.
+  // of this strip's MT x 128 outputs, summing ranks 0..7 in order.
   const int per = (MT * GV_COLS + GV_KSPLIT - 1) / GV_KSPLIT;
   const bool add_bias = (p.epilogue == 1 || p.epilogue == 2);
   const bool relu = (p.epilogue == 2 || p.epilogue == 3);
   for (int j = threadIdx.x; j < per; j += GV_THREADS) {
     const int idx = rank * per + j;
     if (idx >= MT * GV_COLS) break;
-    float s = 0.0f;
+    float sum = 0.0f;
 #pragma unroll
-    for (int q = 0; q < GV_KSPLIT; ++q) s += cluster.map_shared_rank(part, q)[idx];
+    for (int q = 0; q < GV_KSPLIT; ++q) sum += cluster.map_shared_rank(part, q)[idx];
     const int mm = idx / GV_COLS, cc = col0 + (idx - mm * GV_COLS);
     if (mm < p.m && cc < p.n) {
-      if (add_bias) s = __fadd_rn(s, p.bias[cc]);
-      if (relu) s = (s != s) ? s : (s > 0.0f ? s : 0.0f);
-      p.c[mm * p.c_m + cc] = s;
+      if (add_bias) sum = __fadd_rn(sum, p.bias[cc]);
+      if (relu) sum = (sum != sum) ? sum : (sum > 0.0f ? sum : 0.0f);
+      p.c[mm * p.c_m + cc] = sum;
     }
   }
   cluster.sync();  // keep this CTA's `part` alive until every peer has read it

@@ -333,8 +333,10 @@ bool gemv_admission(const Plan& p, const char** why) {
   if (p.batch0 * p.batch1 != 1) { *why = "batched"; return false; }
   if (p.m < 1 || p.m > mmr::GV_MAX_M) { *why = "M outside 1..16"; return false; }
   if (p.k < 1 || p.k > int64_t(mmr::GV_KSPLIT) * mmr::GV_MAX_KSLICE) { *why = "K outside 1..8192"; return false; }
-  if (!(p.b.s_c == 1 && p.b.s_r % 4 == 0 && (p.b.base & 15u) == 0 && p.n % 4 == 0)) {
-    *why = "rhs must be row-major with 16-byte rows and N % 4 == 0";
+  if (p.n > INT32_MAX) { *why = "N too large"; return false; }
+  // B is streamed by TMA: N-contiguous rows with a 16-byte pitch and base.
+  if (!(p.b.s_c == 1 && p.b.s_r % 4 == 0 && p.b.s_r > 0 && (p.b.base & 15u) == 0)) {
+    *why = "rhs must be row-major with 16-byte rows";
     return false;
   }
   if (p.c.s_c != 1 && p.n > 1) { *why = "output columns not contiguous"; return false; }
@@ -367,9 +369,10 @@ EncodeTiledFn encode_fn() {
 // tcgen05 kind::tf32 reads MN-major operands in) when `atom32` is set.
 int32_t encode_3d(CUtensorMap* tm, uint64_t base, uint64_t inner, uint64_t outer, uint64_t batch,
                   int64_t outer_stride_el, int64_t batch_stride_el, uint32_t box_inner, uint32_t box_outer,
-                  const char* name, bool atom32 = false) {
+                  const char* name, bool atom32 = false, bool no_swizzle = false) {
   // A 16-wide (64-byte) box of a K-major operand takes the 64-byte swizzle.
-  const CUtensorMapSwizzle swz = atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+  const CUtensorMapSwizzle swz = no_swizzle ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                 : atom32   ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                                  : box_inner * 4 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(MMR_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -545,7 +548,7 @@ cudaError_t launch_gemv_mt(const mmr_gemm_handle* h, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mmr::gemv_cluster_kernel<MT>, h->gvp);
+  return cudaLaunchKernelEx(&cfg, mmr::gemv_cluster_kernel<MT>, h->tmB, h->gvp);
 }
 
 template <int MT>
@@ -874,17 +877,20 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     g.n = int(p.n);
     g.k = int(p.k);
     int kslice = int((p.k + mmr::GV_KSPLIT - 1) / mmr::GV_KSPLIT);
-    kslice = (kslice + mmr::GV_WARPS - 1) / mmr::GV_WARPS * mmr::GV_WARPS;
+    kslice = (kslice + mmr::GV_ROWS - 1) / mmr::GV_ROWS * mmr::GV_ROWS;
     g.kslice = kslice;
     g.a = reinterpret_cast<const float*>(p.a.base);
     g.a_m = p.a.s_r;
     g.a_k = p.a.s_c;
-    g.b = reinterpret_cast<const float*>(p.b.base);
-    g.b_k = p.b.s_r;
     g.c = reinterpret_cast<float*>(p.c.base);
     g.c_m = p.c.s_r;
     g.bias = reinterpret_cast<const float*>(p.bias);
     g.epilogue = p.epilogue;
+    g.err = h->d_err;
+    g.timeout_ns = h->wait_timeout_ns;
+    if (int32_t e = encode_3d(&h->tmB, p.b.base, p.n, p.k, 1, p.b.s_r, 0, mmr::GV_COLS, mmr::GV_ROWS, "rhs",
+                              false, true))
+      return cleanup(e);
     h->gv_mt = p.m <= 1 ? 1 : p.m <= 2 ? 2 : p.m <= 4 ? 4 : p.m <= 8 ? 8 : 16;
     h->smem = mmr::gemv_smem_bytes(h->gv_mt, kslice);
     h->grid = dim3(unsigned((p.n + mmr::GV_COLS - 1) / mmr::GV_COLS), mmr::GV_KSPLIT, 1);

@@ -73,10 +73,10 @@ def test_unaligned_layouts_fall_back_to_simt_or_reject_forced_family():
         validate(MatMulNode(math_mode=KernelMathMode.Exact, family=KernelFamily.Gemv), a, b, c)
     # padded rows make the same logical shapes TMA-admissible
     a, b, c = fake((5, 7), 1, pad_cols=8), fake((7, 3), 2, pad_cols=4), fake((5, 3), 3, pad_cols=4)
-    # N = 3 is not a whole float4 so GEMV declines; TMA clips the ragged tile
-    assert validate(MatMulNode(), a, b, c)["family"] == 1
-    with pytest.raises(execution.UnsupportedFamily):
-        validate(MatMulNode(family=KernelFamily.Gemv), a, b, c)
+    # M <= 16 with 16-byte rows streams B through the GEMV family (TMA
+    # zero-fills the ragged N edge); the tcgen05 family is admissible too
+    assert validate(MatMulNode(), a, b, c)["family"] == 2
+    assert validate(MatMulNode(family=KernelFamily.Tcgen05), a, b, c)["family"] == 1
 
 
 @pytest.mark.parametrize("lhs,rhs,out,ok", [
