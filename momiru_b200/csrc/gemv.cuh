@@ -45,7 +45,7 @@ struct GemvParams {
 };
 
 // Dynamic shared memory: the stage ring (reused afterwards for the per-warp
-// partials [8][MT][128]), the A slice [MT][kslice], the CTA partial [MT][128]
+// partials [8][MT][128]), the A slice [kslice][MT] (transposed), the CTA partial [MT][128]
 // that cluster peers read, and the ring's barriers.
 __host__ __device__ constexpr int gemv_ring_bytes(int mt) {
   return (GV_STAGES * GV_STAGE_BYTES > GV_CONSUMER_WARPS * mt * GV_COLS * 4)
@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gv_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = base;                                                  // [GV_STAGES][32][128] f32
   float* red = reinterpret_cast<float*>(base);                           // aliases the ring afterwards
-  float* As = reinterpret_cast<float*>(base + gemv_ring_bytes(MT));      // [MT][kslice]
+  float* As = reinterpret_cast<float*>(base + gemv_ring_bytes(MT));      // [kslice][MT]
   float* part = As + MT * p.kslice;                                      // [MT][128]
   uint64_t* full = reinterpret_cast<uint64_t*>(part + MT * GV_COLS);
   uint64_t* empty = full + GV_STAGES;
@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
     // A slice into shared memory while the first stages are in flight; the
     // loads are independent, so issue them back to back (16-byte vectors when
     // A's rows are K-contiguous and aligned).
+    // Stored transposed, As[kk][mm], so that one B row's M multipliers are
+    // contiguous and arrive as MT/4 broadcast 16-byte loads.
     const bool vec = p.a_k == 1 && (p.a_m & 3) == 0 && (k_lo & 3) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.a) & 15u) == 0;
     if (vec) {
@@ -133,14 +135,17 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
             if (gk + 2 < k_hi) v.z = p.a[mm * p.a_m + gk + 2];
           }
         }
-        *reinterpret_cast<float4*>(As + mm * p.kslice + kk) = v;
+        As[(kk + 0) * MT + mm] = v.x;
+        As[(kk + 1) * MT + mm] = v.y;
+        As[(kk + 2) * MT + mm] = v.z;
+        As[(kk + 3) * MT + mm] = v.w;
       }
     } else {
 #pragma unroll 8
       for (int idx = threadIdx.x; idx < MT * p.kslice; idx += GV_CONSUMER_WARPS * 32) {
         const int mm = idx / p.kslice, kk = idx - mm * p.kslice;
         const int gk = k_lo + kk;
-        As[idx] = (mm < p.m && gk < k_hi) ? p.a[mm * p.a_m + gk * p.a_k] : 0.0f;
+        As[kk * MT + mm] = (mm < p.m && gk < k_hi) ? p.a[mm * p.a_m + gk * p.a_k] : 0.0f;
       }
     }
     asm volatile("bar.sync 1, %0;" ::"n"(GV_CONSUMER_WARPS * 32) : "memory");  // consumers only
@@ -156,21 +161,30 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
       const int slot = s % GV_STAGES;
       const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
       if (!mbar_wait(&full[slot], phase, ctl, kDevTimeoutFull)) break;
-      const uint8_t* st = ring + slot * GV_STAGE_BYTES;
+      const uint8_t* st = ring + slot * GV_STAGE_BYTES + warp * 4 * (GV_COLS * 4) + lane * 16;
+      const int kk0 = s * GV_ROWS + warp * 4;  // row offset within the slice
+      const float* a0 = As + kk0 * MT;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int row = warp * 4 + r;
-        const int k = k_lo + s * GV_ROWS + row;
-        if (k < k_hi) {
-          const float4 bv = *reinterpret_cast<const float4*>(st + row * (GV_COLS * 4) + lane * 16);
-          const float* arow = As + (k - k_lo);
+        if (k_lo + kk0 + r < k_hi) {
+          const float4 bv = *reinterpret_cast<const float4*>(st + r * (GV_COLS * 4));
+          float av[MT];
+          if constexpr (MT >= 4) {
+#pragma unroll
+            for (int i = 0; i < MT; i += 4) {
+              const float4 a4 = *reinterpret_cast<const float4*>(a0 + r * MT + i);
+              av[i] = a4.x; av[i + 1] = a4.y; av[i + 2] = a4.z; av[i + 3] = a4.w;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < MT; ++i) av[i] = a0[r * MT + i];
+          }
 #pragma unroll
           for (int i = 0; i < MT; ++i) {
-            const float av = arow[i * p.kslice];
-            acc[i][0] = fmaf(av, bv.x, acc[i][0]);
-            acc[i][1] = fmaf(av, bv.y, acc[i][1]);
-            acc[i][2] = fmaf(av, bv.z, acc[i][2]);
-            acc[i][3] = fmaf(av, bv.w, acc[i][3]);
+            acc[i][0] = fmaf(av[i], bv.x, acc[i][0]);
+            acc[i][1] = fmaf(av[i], bv.y, acc[i][1]);
+            acc[i][2] = fmaf(av[i], bv.z, acc[i][2]);
+            acc[i][3] = fmaf(av[i], bv.w, acc[i][3]);
           }
         }
       }
