@@ -476,7 +476,7 @@ cudaError_t prepare_tc(int smem) {
   return cudaSuccess;
 }
 
-template <bool AMN, bool BMN>
+template <int MODE, bool AMN, bool BMN>
 cudaError_t launch_tc2(mmr_gemm_handle* h, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = h->grid;
@@ -490,17 +490,17 @@ cudaError_t launch_tc2(mmr_gemm_handle* h, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mmr::tc_gemm_2sm_kernel<AMN, BMN>, h->tmA, h->tmB, h->tmC, h->tcp);
+  return cudaLaunchKernelEx(&cfg, mmr::tc_gemm_2sm_kernel<MODE, AMN, BMN>, h->tmA, h->tmB, h->tmC, h->tcp);
 }
 
-template <bool AMN, bool BMN>
+template <int MODE, bool AMN, bool BMN>
 cudaError_t prepare_tc2(int smem) {
-  using Cfg = mmr::Tc2Config;
-  cudaError_t e = cudaFuncSetAttribute(mmr::tc_gemm_2sm_kernel<AMN, BMN>,
+  using Cfg = mmr::Tc2Config<MODE>;
+  cudaError_t e = cudaFuncSetAttribute(mmr::tc_gemm_2sm_kernel<MODE, AMN, BMN>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaFuncAttributes fa;
-  e = cudaFuncGetAttributes(&fa, mmr::tc_gemm_2sm_kernel<AMN, BMN>);
+  e = cudaFuncGetAttributes(&fa, mmr::tc_gemm_2sm_kernel<MODE, AMN, BMN>);
   if (e != cudaSuccess) return e;
   const long need = 2L * 128 * Cfg::kEpiRegs + long(Cfg::kThreads - 256) * Cfg::kOtherRegs;
   if (long(fa.numRegs) * Cfg::kThreads < need) return cudaErrorInvalidConfiguration;
@@ -516,15 +516,17 @@ TcLaunch tc_launch_table(int mode, bool amn, bool bmn) {
       {{launch_tc<1, false, false>, launch_tc<1, false, true>}, {launch_tc<1, true, false>, launch_tc<1, true, true>}}};
   return t[mode][amn][bmn];
 }
-TcLaunch tc2_launch_table(bool amn, bool bmn) {
-  static const TcLaunch t[2][2] = {{launch_tc2<false, false>, launch_tc2<false, true>},
-                                   {launch_tc2<true, false>, launch_tc2<true, true>}};
-  return t[amn][bmn];
+TcLaunch tc2_launch_table(int mode, bool amn, bool bmn) {
+  static const TcLaunch t[2][2][2] = {
+      {{launch_tc2<0, false, false>, launch_tc2<0, false, true>}, {launch_tc2<0, true, false>, launch_tc2<0, true, true>}},
+      {{launch_tc2<1, false, false>, launch_tc2<1, false, true>}, {launch_tc2<1, true, false>, launch_tc2<1, true, true>}}};
+  return t[mode][amn][bmn];
 }
-TcPrep tc2_prep_table(bool amn, bool bmn) {
-  static const TcPrep t[2][2] = {{prepare_tc2<false, false>, prepare_tc2<false, true>},
-                                 {prepare_tc2<true, false>, prepare_tc2<true, true>}};
-  return t[amn][bmn];
+TcPrep tc2_prep_table(int mode, bool amn, bool bmn) {
+  static const TcPrep t[2][2][2] = {
+      {{prepare_tc2<0, false, false>, prepare_tc2<0, false, true>}, {prepare_tc2<0, true, false>, prepare_tc2<0, true, true>}},
+      {{prepare_tc2<1, false, false>, prepare_tc2<1, false, true>}, {prepare_tc2<1, true, false>, prepare_tc2<1, true, true>}}};
+  return t[mode][amn][bmn];
 }
 
 TcPrep tc_prep_table(int mode, bool amn, bool bmn) {
@@ -801,12 +803,13 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
   const int64_t batch = p.batch0 * p.batch1;
   if (fam == MMR_FAMILY_TCGEN05) {
     h->mode = (p.math == MMR_MATH_STRICT_FP32) ? 1 : 0;
-    // StrictFp32 runs on CTA pairs (256-row tiles) unless M fits one 128-row tile.
-    h->pair = h->mode == 1 && p.m > mmr::TC_BM;
+    // Both modes run on CTA pairs (256-row tiles) unless M fits one 128-row tile.
+    h->pair = p.m > mmr::TC_BM;
     h->a_mn = t.a_mn;
     h->b_mn = t.b_mn;
-    const uint32_t bk = h->pair ? uint32_t(mmr::Tc2Config::kBK)
-                                : (h->mode ? mmr::TcConfig<1>::kBK : mmr::TcConfig<0>::kBK);
+    const uint32_t bk = h->mode ? mmr::TcConfig<1>::kBK : mmr::TcConfig<0>::kBK;
+    static_assert(mmr::TcConfig<1>::kBK == mmr::Tc2Config<1>::kBK && mmr::TcConfig<0>::kBK == mmr::Tc2Config<0>::kBK,
+                  "one k-block width per mode");
     const int tile_m = h->pair ? 2 * mmr::TC_BM : mmr::TC_BM;
     int32_t e = encode_tc_maps(h, p, t, batch, bk, h->pair ? 128u : uint32_t(mmr::TC_BN));
     if (e) return cleanup(e);
@@ -847,12 +850,12 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     h->sms = sms;
     cudaError_t ce;
     if (h->pair) {
-      h->smem = mmr::Tc2Config::kSmemBytes;
+      h->smem = h->mode ? mmr::Tc2Config<1>::kSmemBytes : mmr::Tc2Config<0>::kSmemBytes;
       h->grid = dim3(unsigned(2 * std::min<int64_t>(tiles, sms / 2)));
-      h->block = dim3(mmr::Tc2Config::kThreads);
-      ce = tc2_prep_table(t.a_mn, t.b_mn)(h->smem);
+      h->block = dim3(h->mode ? mmr::Tc2Config<1>::kThreads : mmr::Tc2Config<0>::kThreads);
+      ce = tc2_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
       h->info.cluster = 2;
-      h->info.stages = mmr::Tc2Config::kStages;
+      h->info.stages = mmr::Tc2Config<1>::kStages;
     } else {
       h->smem = h->mode ? mmr::TcConfig<1>::kSmemBytes : mmr::TcConfig<0>::kSmemBytes;
       h->grid = dim3(unsigned(std::min<int64_t>(tiles, sms)));
@@ -965,7 +968,7 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
   if (!h->plan.empty) {
     switch (h->family) {
       case MMR_FAMILY_TCGEN05:
-        e = h->pair ? tc2_launch_table(h->a_mn, h->b_mn)(h, s) : tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s);
+        e = h->pair ? tc2_launch_table(h->mode, h->a_mn, h->b_mn)(h, s) : tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s);
         if (e == cudaSuccess && h->mode == 1) {
           mmr::tc_nonfinite_fixup_kernel<<<h->sms, 256, 0, s>>>(h->sp, h->tcp);
           e = cudaGetLastError();

@@ -96,6 +96,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// 3-D tiled load into this CTA's shared memory whose completion bytes are
+// counted on the even CTA's mbarrier of the pair (`cluster_bar` is that
+// barrier's cluster address). Not a multicast: each CTA loads its own tile.
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* tm, uint32_t cluster_bar, int c0,
+                                                 int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(cluster_bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
 // 3-D tiled store shared -> global (clipped to the tensor bounds by TMA).
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, const void* src, int c0, int c1, int c2) {
   asm volatile(

@@ -1,16 +1,20 @@
-// tc_gemm_2sm.cuh -- 3xTF32 f32 GEMM on CTA pairs (tcgen05 cta_group::2).
+// tc_gemm_2sm.cuh -- f32 GEMM on CTA pairs (tcgen05 cta_group::2), in both
+// numeric modes: MODE 1 = StrictFp32 (3xTF32), MODE 0 = one TF32 pass.
 //
-// Same contract and numerics as tc_gemm_kernel<1, ...> (StrictFp32: 3xTF32
-// split, 256-wide K chunks summed with round-to-nearest adds, exact fix-up
-// of tiles with inf/NaN inputs), but each output tile of 256 x 256 is
+// Same contract and numerics as tc_gemm_kernel<MODE, ...> (3xTF32 split,
+// 256-wide K chunks summed with round-to-nearest adds, exact fix-up of tiles
+// with inf/NaN inputs; TF32 keeps one chain per tile), but each output tile
+// of 256 x 256 is
 // computed by a cluster of two CTAs on two SMs with one 256-row MMA per
 // k-step. Each CTA stages only its 128 rows of A and its 128-column half of
 // B (plus their lo parts), which halves the per-SM shared-memory traffic of
 // the B operand -- the bound of the one-CTA 3xTF32 kernel.
 //
 // Pair protocol (rank 0 = even CTA issues every MMA of the pair):
-//   full[s]        local, TMA -> split warps of the same CTA
-//   split_done[s]  rank 0 only, 12 arrivals: six split warps of each CTA
+//   full[s]        3xTF32: local, TMA -> split warps of the same CTA.
+//                  TF32: rank 0's counts the bytes of both CTAs' loads (the
+//                  odd CTA's loads name it) and gates the MMA directly.
+//   split_done[s]  3xTF32, rank 0 only, 12 arrivals: six split warps of each CTA
 //   empty[s]       each CTA, one arrival from rank 0's tcgen05.commit
 //   acc_full[a]    each CTA, one arrival from rank 0's tcgen05.commit
 //   acc_empty[a]   rank 0 only, 16 arrivals: eight epilogue warps of each CTA
@@ -22,31 +26,34 @@
 
 namespace mmr {
 
+template <int MODE>
 struct Tc2Config {
-  static constexpr int kBK = 16;
+  static constexpr int kBK = MODE ? 16 : 32;
   static constexpr int kABytes = 128 * kBK * 4;          // this CTA's 128 rows of A
   static constexpr int kBBytes = 128 * kBK * 4;          // this CTA's 128 columns of B
-  static constexpr int kStageBytes = kABytes + kBBytes;  // 16 KiB raw (+16 KiB lo)
+  static constexpr int kStageBytes = kABytes + kBBytes;  // raw operands (+ as much again for lo)
   static constexpr int kStages = 6;
-  static constexpr int kWarps = 16;
+  static constexpr int kWarps = MODE ? 16 : 12;
   static constexpr int kThreads = 32 * kWarps;
-  static constexpr int kLaunchRegs = 128;
-  static constexpr int kEpiRegs = 176;
-  static constexpr int kOtherRegs = 80;
-  static constexpr int kOperandBytes = kStages * kStageBytes * 2;
+  static constexpr int kLaunchRegs = MODE ? 128 : 168;
+  static constexpr int kEpiRegs = MODE ? 176 : 200;
+  static constexpr int kOtherRegs = MODE ? 80 : 96;
+  static constexpr int kOperandBytes = kStages * kStageBytes * (MODE ? 2 : 1);
   static constexpr int kCstageBytes = TC_EPI_WARPS * TC_CSTAGE_BYTES;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kSmemBytes = kOperandBytes + kCstageBytes + kBarrierBytes + 1024;
-  static constexpr uint32_t kMnAtomBytes = kBK * 128u;   // 32 MN elements x 16 K rows
+  static constexpr uint32_t kMnAtomBytes = kBK * 128u;   // 32 MN elements x kBK K rows
+  static constexpr uint32_t kKmajLayout = kBK == 32 ? 2u : 4u;
+  static constexpr uint32_t kKmajSbo = 8u * kBK * 4u;
   static_assert(2 * 128 * kEpiRegs + (kWarps - 8) * 32 * kOtherRegs <= kThreads * kLaunchRegs,
                 "register split exceeds the launch budget");
 };
 
-template <bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(Tc2Config::kThreads, 1)
+template <int MODE, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
     tc_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const TcParams p) {
-  using Cfg = Tc2Config;
+  using Cfg = Tc2Config<MODE>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -192,6 +199,7 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
         int issued_parity[S];
         for (int s = 0; s < S; ++s) issued_parity[s] = -1;
         bool ok = true;
+        const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
         for (int t = pair; ok && t < p.tiles_total; t += npairs) {
           int mt, nt, bt;
           tc_tile_coords(p, t, mt, nt, bt);
@@ -203,28 +211,56 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
             uint8_t* sa = ops + stage * Cfg::kStageBytes;
             uint8_t* sb = sa + Cfg::kABytes;
             const int k0 = kb * Cfg::kBK;
-            mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
-            if (A_MN) {
+            if (MODE) {
+              // 3xTF32: each CTA's loads complete on its own barrier; the
+              // split warps gate the MMA.
+              mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+              if (A_MN) {
 #pragma unroll
-              for (int i = 0; i < 4; ++i) tma_load_3d(sa + i * Cfg::kMnAtomBytes, &tmA, &full[stage], m0 + 32 * i, k0, ba);
-            } else {
-              tma_load_3d(sa, &tmA, &full[stage], k0, m0, ba);
-            }
-            if (B_MN) {
+                for (int i = 0; i < 4; ++i)
+                  tma_load_3d(sa + i * Cfg::kMnAtomBytes, &tmA, &full[stage], m0 + 32 * i, k0, ba);
+              } else {
+                tma_load_3d(sa, &tmA, &full[stage], k0, m0, ba);
+              }
+              if (B_MN) {
 #pragma unroll
-              for (int j = 0; j < 4; ++j) tma_load_3d(sb + j * Cfg::kMnAtomBytes, &tmB, &full[stage], nb + 32 * j, k0, bb);
+                for (int j = 0; j < 4; ++j)
+                  tma_load_3d(sb + j * Cfg::kMnAtomBytes, &tmB, &full[stage], nb + 32 * j, k0, bb);
+              } else {
+                tma_load_3d(sb, &tmB, &full[stage], k0, nb, bb);
+              }
             } else {
-              tma_load_3d(sb, &tmB, &full[stage], k0, nb, bb);
+              // TF32: both CTAs' loads complete on the even CTA's barrier,
+              // which expects the bytes of the pair.
+              const uint32_t fbar = full_leader0 + 8u * stage;
+              if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+              if (A_MN) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  tma_load_3d_pair(sa + i * Cfg::kMnAtomBytes, &tmA, fbar, m0 + 32 * i, k0, ba);
+              } else {
+                tma_load_3d_pair(sa, &tmA, fbar, k0, m0, ba);
+              }
+              if (B_MN) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                  tma_load_3d_pair(sb + j * Cfg::kMnAtomBytes, &tmB, fbar, nb + 32 * j, k0, bb);
+              } else {
+                tma_load_3d_pair(sb, &tmB, fbar, k0, nb, bb);
+              }
             }
             issued_parity[stage] = static_cast<int>(phase);
             if (++stage == S) { stage = 0; phase ^= 1u; }
           }
         }
-        for (int s = 0; s < S; ++s) {
+        // Every load this CTA issued must have landed before it may exit. In
+        // TF32 mode the odd CTA's loads count on the even CTA's barrier, which
+        // the even CTA drains; the closing cluster barrier covers the pair.
+        for (int s = 0; (MODE || rank == 0) && s < S; ++s) {
           if (issued_parity[s] >= 0) {
             const uint32_t a = smem_u32(&full[s]);
             const uint64_t t0 = globaltimer_ns();
-            while (!mbar_try_wait(a, static_cast<uint32_t>(issued_parity[s]))) {
+            while (!mbar_try_wait_cluster(a, static_cast<uint32_t>(issued_parity[s]))) {
               if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
             }
           }
@@ -234,9 +270,9 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
       if (lane == 0 && rank == 0) {
         // ----------------------------------------------- MMA issuer (pair)
         constexpr uint32_t idesc = idesc_tf32(256, TC_BN, A_MN, B_MN);
-        constexpr uint32_t a_layout = A_MN ? 1u : 4u, b_layout = B_MN ? 1u : 4u;
-        constexpr uint32_t a_lbo = A_MN ? Cfg::kMnAtomBytes : 16u, a_sbo = 512u;
-        constexpr uint32_t b_lbo = B_MN ? Cfg::kMnAtomBytes : 16u, b_sbo = 512u;
+        constexpr uint32_t a_layout = A_MN ? 1u : Cfg::kKmajLayout, b_layout = B_MN ? 1u : Cfg::kKmajLayout;
+        constexpr uint32_t a_lbo = A_MN ? Cfg::kMnAtomBytes : 16u, a_sbo = A_MN ? 512u : Cfg::kKmajSbo;
+        constexpr uint32_t b_lbo = B_MN ? Cfg::kMnAtomBytes : 16u, b_sbo = B_MN ? 512u : Cfg::kKmajSbo;
         constexpr uint32_t a_kstep = A_MN ? 1024u : 32u, b_kstep = B_MN ? 1024u : 32u;
         const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), 1);
         const uint32_t acc_full_peer0 = mapa_shared(smem_u32(&acc_full[0]), 1);
@@ -255,7 +291,8 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
               tc_fence_after();
               d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
             }
-            if (!mbar_wait_cluster(&split_done[stage], phase, ctl, kDevTimeoutXform)) { ok = false; break; }
+            uint64_t* ready = MODE ? &split_done[stage] : &full[stage];
+            if (!mbar_wait_cluster(ready, phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) { ok = false; break; }
             tc_fence_after();
             const uint32_t sa = smem_u32(ops + stage * Cfg::kStageBytes);
             const uint32_t sb = sa + Cfg::kABytes;
@@ -265,11 +302,15 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
             for (int kk = 0; kk < Cfg::kBK / 8; ++kk) {
               const uint64_t ad = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_layout);
               const uint64_t bd = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_layout);
-              const uint64_t ad_lo = smem_desc(sa_lo + kk * a_kstep, a_lbo, a_sbo, a_layout);
-              const uint64_t bd_lo = smem_desc(sb_lo + kk * b_kstep, b_lbo, b_sbo, b_layout);
-              umma_tf32_2sm(d_tmem, ad_lo, bd, idesc, (kc | kk) != 0);
-              umma_tf32_2sm(d_tmem, ad, bd_lo, idesc, 1u);
-              umma_tf32_2sm(d_tmem, ad, bd, idesc, 1u);
+              if (MODE) {
+                const uint64_t ad_lo = smem_desc(sa_lo + kk * a_kstep, a_lbo, a_sbo, a_layout);
+                const uint64_t bd_lo = smem_desc(sb_lo + kk * b_kstep, b_lbo, b_sbo, b_layout);
+                umma_tf32_2sm(d_tmem, ad_lo, bd, idesc, (kc | kk) != 0);
+                umma_tf32_2sm(d_tmem, ad, bd_lo, idesc, 1u);
+                umma_tf32_2sm(d_tmem, ad, bd, idesc, 1u);
+              } else {
+                umma_tf32_2sm(d_tmem, ad, bd, idesc, (kc | kk) != 0);
+              }
             }
             issued_any = true;
             umma_commit_2sm(smem_u32(&empty[stage]));
@@ -294,7 +335,7 @@ __global__ void __launch_bounds__(Tc2Config::kThreads, 1)
           }
         }
       }
-    } else if (warp >= TC_SPLIT_WARP0 && warp < TC_SPLIT_WARP0 + TC_SPLIT_WARPS) {
+    } else if (MODE && warp >= TC_SPLIT_WARP0 && warp < TC_SPLIT_WARP0 + TC_SPLIT_WARPS) {
       // ------------------------------------------------------- split warps
       const int tid = threadIdx.x - TC_SPLIT_WARP0 * 32;
       const uint32_t split_done_leader0 = mapa_shared(smem_u32(&split_done[0]), 0);
