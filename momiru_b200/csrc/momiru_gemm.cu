@@ -423,6 +423,9 @@ struct mmr_gemm_handle {
   int* d_err = nullptr;
   int* h_err = nullptr;  // pinned host copy of the error word
   unsigned int* d_nf = nullptr;  // 3xTF32 non-finite bookkeeping
+  float* d_ws = nullptr;         // stream-K partial sums (CTA pairs)
+  unsigned int* d_ws_flag = nullptr;
+  size_t ws_flag_bytes = 0;
   int sms = 148;
   // column-sharded GEMM with replicated output
   bool sharded = false;
@@ -851,7 +854,25 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     cudaError_t ce;
     if (h->pair) {
       h->smem = h->mode ? mmr::Tc2Config<1>::kSmemBytes : mmr::Tc2Config<0>::kSmemBytes;
-      h->grid = dim3(unsigned(2 * std::min<int64_t>(tiles, sms / 2)));
+      const int64_t npairs = std::min<int64_t>(tiles, sms / 2);
+      h->grid = dim3(unsigned(2 * npairs));
+      // Stream-K workspace: two partial-sum slots per pair, and an arrival
+      // counter per split tile (fewer than two rounds of them) and epilogue
+      // warp of each CTA.
+      const size_t ws_bytes = size_t(npairs) * 2 * mmr::kSkSlotFloats * sizeof(float);
+      h->ws_flag_bytes = size_t(2 * npairs) * 2 * mmr::TC_EPI_WARPS * sizeof(unsigned int);
+      if (cudaMalloc(&h->d_ws, ws_bytes) != cudaSuccess ||
+          cudaMalloc(&h->d_ws_flag, h->ws_flag_bytes) != cudaSuccess ||
+          cudaMemset(h->d_ws_flag, 0, h->ws_flag_bytes) != cudaSuccess)
+        return cleanup(fail(MMR_ERR_CUDA, "allocating the stream-K workspace failed"));
+      q.ws = h->d_ws;
+      q.ws_flag = h->d_ws_flag;
+      // Whole rounds of tiles stay round-robin. When the tiles do not fill
+      // the last round, that round is split stream-K; when it is less than
+      // half full, the round before it is split too, so that no tile is cut
+      // into more pieces than about three pairs.
+      const int64_t rem = tiles % npairs;
+      q.sk_tiles = rem == 0 ? 0 : int(2 * rem >= npairs ? rem : npairs + rem);
       h->block = dim3(h->mode ? mmr::Tc2Config<1>::kThreads : mmr::Tc2Config<0>::kThreads);
       ce = tc2_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
       h->info.cluster = 2;
@@ -1033,6 +1054,8 @@ int32_t mmr_gemm_quiesce(mmr_gemm_handle* h, uint64_t timeout_ns) {
   if (code != 0) {
     *h->h_err = 0;
     cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
+    // A run that gave up may leave stream-K arrival counts that nothing reset.
+    if (h->d_ws_flag) cudaMemsetAsync(h->d_ws_flag, 0, h->ws_flag_bytes, h->stream);
     return fail(code == mmr::kDevTimeoutDrain || code <= mmr::kDevTimeoutXform || code == mmr::kDevTimeoutPeer
                     ? MMR_ERR_TIMEOUT
                     : MMR_ERR_DEVICE_FAULT_FLAG,
@@ -1051,6 +1074,8 @@ int32_t mmr_gemm_destroy(mmr_gemm_handle* h) {
     if (h->err_ev) cudaEventDestroy(h->err_ev);
     if (h->d_err) cudaFree(h->d_err);
     if (h->d_nf) cudaFree(h->d_nf);
+    if (h->d_ws) cudaFree(h->d_ws);
+    if (h->d_ws_flag) cudaFree(h->d_ws_flag);
     if (h->h_err) cudaFreeHost(h->h_err);
   }
   delete h;

@@ -111,6 +111,11 @@ struct TcParams {
   // peer_c[i] as from c (addresses mapped into this process).
   int npeers;
   float* peer_c[kMaxPeers];
+  // Stream-K partial sums (CTA-pair kernel): two slots per pair, and arrival
+  // counters per split tile and epilogue warp of each CTA (zero between launches).
+  float* ws;
+  unsigned int* ws_flag;
+  int sk_tiles;  // trailing tiles split stream-K style (0: whole tiles only)
 };
 
 // Copies one finished 32x32 box from the 128B-swizzled staging buffer to each

@@ -3,12 +3,23 @@
 //
 // Same contract and numerics as tc_gemm_kernel<MODE, ...> (3xTF32 split,
 // 256-wide K chunks summed with round-to-nearest adds, exact fix-up of tiles
-// with inf/NaN inputs; TF32 keeps one chain per tile), but each output tile
-// of 256 x 256 is
-// computed by a cluster of two CTAs on two SMs with one 256-row MMA per
-// k-step. Each CTA stages only its 128 rows of A and its 128-column half of
-// B (plus their lo parts), which halves the per-SM shared-memory traffic of
-// the B operand -- the bound of the one-CTA 3xTF32 kernel.
+// with inf/NaN inputs; TF32 keeps one chain per tile segment), but each output
+// tile of 256 x 256 is computed by a cluster of two CTAs on two SMs with one
+// 256-row MMA per k-step. Each CTA stages only its 128 rows of A and its
+// 128-column half of B (plus their lo parts), which halves the per-SM
+// shared-memory traffic of the B operand.
+//
+// Work split: whole tiles round-robin, except the last sk_tiles (the partial
+// last round, or the last two rounds when that one is under half full), whose
+// k-blocks, in tile-major order, are dealt to the pairs in equal contiguous
+// ranges (stream-K), so no pair idles in a last partial round of tiles. A
+// range is a list of segments (tile, k-blocks [kb0, kb1)): a whole tile goes
+// through the epilogue as usual; a part of a split tile parks its partial sum
+// in a workspace slot of its pair and counts itself in on a per-tile counter
+// (one per epilogue warp). The warp whose part completes the count adds the
+// parts in K order with round-to-nearest adds (so the result is the same
+// whichever pair arrives last), stores the tile and resets the counter.
+// Nothing waits on another pair, so the pairs need not be co-resident.
 //
 // Pair protocol (rank 0 = even CTA issues every MMA of the pair):
 //   full[s]        3xTF32: local, TMA -> split warps of the same CTA.
@@ -47,6 +58,77 @@ struct Tc2Config {
   static constexpr uint32_t kKmajSbo = 8u * kBK * 4u;
   static_assert(2 * 128 * kEpiRegs + (kWarps - 8) * 32 * kOtherRegs <= kThreads * kLaunchRegs,
                 "register split exceeds the launch budget");
+};
+
+// Floats of one partial-sum slot: two CTAs x 128 rows x 256 columns.
+constexpr int kSkSlotFloats = 2 * 128 * TC_BN;
+
+// The first tiles_total - sk_tiles tiles are whole tiles dealt round-robin
+// (tile = pair + i * npairs), so the pairs running at one time share A and B
+// panels in L2; only the last sk_tiles tiles are split stream-K style.
+// Equal contiguous ranges of the stream-K (tile, k-block) iteration space:
+__device__ __forceinline__ long long sk_unit(const TcParams& p, int pair, int npairs) {
+  const long long U = (long long)p.sk_tiles * p.k_blocks;
+  return (U / npairs) * pair + (U % npairs) * pair / npairs;
+}
+
+// Arrival counter of warp w of CTA `rank` for stream-K tile ts (0-based in
+// the split region): each part's warp adds one after parking its partial sum;
+// the warp that completes the count finishes the tile and resets it to zero.
+__device__ __forceinline__ int sk_counter(int ts, uint32_t rank, int w) {
+  return (2 * ts + static_cast<int>(rank)) * TC_EPI_WARPS + w;
+}
+
+// The pair whose stream-K range holds unit u.
+__device__ __forceinline__ int sk_pair_of(const TcParams& p, long long u, int npairs) {
+  const long long U = (long long)p.sk_tiles * p.k_blocks;
+  int q = static_cast<int>((u * npairs) / U);
+  while (q + 1 < npairs && sk_unit(p, q + 1, npairs) <= u) ++q;
+  while (q > 0 && sk_unit(p, q, npairs) > u) --q;
+  return q;
+}
+
+// One pair's work: its round-robin whole tiles, then its stream-K segments.
+// Odd pairs take their segments last-first. Then the tile split between an odd
+// pair and the even pair after it has both parts computed first and is
+// finished in mid-kernel, instead of at the end where every pair's last tile
+// would otherwise land at once (the replicated output leaves over NVLink tile
+// by tile, so a burst at the end is time that nothing overlaps).
+struct PairWork {
+  int pair, npairs, i, dp_rounds, sk_base, kb_per_tile;
+  long long u0, u1;
+  bool reverse;
+  __device__ __forceinline__ PairWork(const TcParams& p, int pair_, int npairs_)
+      : pair(pair_), npairs(npairs_), i(0), dp_rounds((p.tiles_total - p.sk_tiles) / npairs_),
+        sk_base(p.tiles_total - p.sk_tiles), kb_per_tile(p.k_blocks),
+        u0(sk_unit(p, pair_, npairs_)), u1(sk_unit(p, pair_ + 1, npairs_)), reverse(pair_ & 1) {}
+  __device__ __forceinline__ bool next(int& t, int& kb0, int& kb1) {
+    if (i < dp_rounds) {
+      t = pair + i * npairs;
+      ++i;
+      kb0 = 0;
+      kb1 = kb_per_tile;
+      return true;
+    }
+    if (u0 >= u1) return false;
+    int ts;
+    if (!reverse) {
+      ts = static_cast<int>(u0 / kb_per_tile);
+      kb0 = static_cast<int>(u0 - (long long)ts * kb_per_tile);
+      const long long rem = u1 - u0;
+      kb1 = rem < kb_per_tile - kb0 ? kb0 + static_cast<int>(rem) : kb_per_tile;
+      u0 += kb1 - kb0;
+    } else {
+      ts = static_cast<int>((u1 - 1) / kb_per_tile);
+      const long long tile_u = (long long)ts * kb_per_tile;
+      const long long lo = u0 > tile_u ? u0 : tile_u;
+      kb0 = static_cast<int>(lo - tile_u);
+      kb1 = static_cast<int>(u1 - tile_u);
+      u1 = lo;
+    }
+    t = sk_base + ts;
+    return true;
+  }
 };
 
 template <int MODE, bool A_MN, bool B_MN>
@@ -103,7 +185,6 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
   cluster_sync_all();  // barrier inits and both TMEM allocations visible to the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int n_chunks = (p.k_blocks + p.chunk_kb - 1) / p.chunk_kb;
 
   if (warp < TC_EPI_WARPS) {
     reg_alloc<Cfg::kEpiRegs>();
@@ -115,37 +196,19 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
     const bool add_bias = (p.epilogue == EPI_BIAS || p.epilogue == EPI_BIAS_RELU);
     const bool relu = (p.epilogue == EPI_BIAS_RELU || p.epilogue == EPI_RELU);
     const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
-    bool ok = true;
-    for (int t = pair; ok && t < p.tiles_total; t += npairs) {
+    // This thread's 128 columns of its row inside a partial-sum slot.
+    const int ws_off = static_cast<int>(rank) * 128 * TC_BN + (quarter * 32 + lane) * TC_BN + half * 128;
+    float sum[128];
+
+    // Applies bias/ReLU to sum[] and stores this thread's part of tile t.
+    auto store_tile = [&](int t) {
       int mt, nt, bt;
       tc_tile_coords(p, t, mt, nt, bt);
-      const int m0 = mt * 256 + static_cast<int>(rank) * 128, n0 = nt * TC_BN;
-      float sum[128];
-#pragma unroll
-      for (int i = 0; i < 128; ++i) sum[i] = 0.0f;
-      for (int c = 0; c < n_chunks; ++c) {
-        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, ctl, kDevTimeoutAcc)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t tb = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                            static_cast<uint32_t>(acc * TC_BN + half * 128);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tb + j * 32, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sum[j * 32 + i] = __fadd_rn(sum[j * 32 + i], __uint_as_float(r[i]));
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(acc_empty_leader0 + 8u * acc);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-      }
-      if (!ok) break;
-      const int row0 = m0 + quarter * 32;
+      const int row0 = mt * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+      const int nbase = nt * TC_BN + half * 128;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int col0 = n0 + half * 128 + j * 32;
+        const int col0 = nbase + j * 32;
         float bias_lane = 0.0f;
         if (add_bias && col0 + lane < p.n) bias_lane = __ldg(p.bias + col0 + lane);
         float* v = sum + j * 32;
@@ -185,6 +248,76 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
         }
         if (p.npeers) store_box_to_peers(p, buf, row0, col0, bt, lane);
       }
+    };
+    auto save_partial = [&](float* slot) {
+      float4* dst = reinterpret_cast<float4*>(slot + ws_off);
+#pragma unroll
+      for (int q = 0; q < 32; ++q) dst[q] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
+    };
+
+    bool ok = true;
+    PairWork segs(p, pair, npairs);
+    int t, kb0, kb1;
+    while (ok && segs.next(t, kb0, kb1)) {
+#pragma unroll
+      for (int i = 0; i < 128; ++i) sum[i] = 0.0f;
+      const int n_chunks = (kb1 - kb0 + p.chunk_kb - 1) / p.chunk_kb;
+      for (int c = 0; c < n_chunks; ++c) {
+        if (!mbar_wait_cluster(&acc_full[acc], acc_phase, ctl, kDevTimeoutAcc)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t tb = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                            static_cast<uint32_t>(acc * TC_BN + half * 128);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tb + j * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sum[j * 32 + i] = __fadd_rn(sum[j * 32 + i], __uint_as_float(r[i]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(acc_empty_leader0 + 8u * acc);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+      if (!ok) break;
+      if (kb0 == 0 && kb1 == p.k_blocks) {
+        store_tile(t);
+        continue;
+      }
+      // One part of a split tile: park it (slot 0 for the part that ends the
+      // tile's K range, slot 1 for a head or middle part), then count it in.
+      const int ts = t - (p.tiles_total - p.sk_tiles);
+      save_partial(p.ws + (2 * pair + (kb1 == p.k_blocks ? 0 : 1)) * kSkSlotFloats);
+      __threadfence();
+      __syncwarp();
+      const int q0 = sk_pair_of(p, (long long)ts * p.k_blocks, npairs);
+      const int q1 = sk_pair_of(p, (long long)(ts + 1) * p.k_blocks - 1, npairs);
+      unsigned int last = 0;
+      if (lane == 0) {
+        unsigned int* cnt = p.ws_flag + sk_counter(ts, rank, warp);
+        unsigned int before;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(cnt) : "memory");
+        last = before == static_cast<unsigned int>(q1 - q0);
+        if (last) *cnt = 0u;  // every part has arrived: ready for the next launch
+      }
+      if (!__shfl_sync(0xffffffffu, last, 0)) continue;
+      // Last part in: add the parts in K order (pairs q0 .. q1) with
+      // round-to-nearest adds, whichever pair finishes, and store the tile.
+#pragma unroll
+      for (int i = 0; i < 128; ++i) sum[i] = 0.0f;
+      for (int q = q0; q <= q1; ++q) {
+        const float* src = p.ws + (2 * q + (q == q1 ? 0 : 1)) * kSkSlotFloats + ws_off;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
+          sum[4 * i] = __fadd_rn(sum[4 * i], v.x);
+          sum[4 * i + 1] = __fadd_rn(sum[4 * i + 1], v.y);
+          sum[4 * i + 2] = __fadd_rn(sum[4 * i + 2], v.z);
+          sum[4 * i + 3] = __fadd_rn(sum[4 * i + 3], v.w);
+        }
+      }
+      store_tile(t);
     }
     if (lane == 0) bulk_wait_group_all();
     if (p.npeers) __threadfence_system();  // peer stores ordered before the completion signal
@@ -200,13 +333,15 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
         for (int s = 0; s < S; ++s) issued_parity[s] = -1;
         bool ok = true;
         const uint32_t full_leader0 = mapa_shared(smem_u32(&full[0]), 0);
-        for (int t = pair; ok && t < p.tiles_total; t += npairs) {
+        PairWork segs(p, pair, npairs);
+        int t, kb0, kb1;
+        while (ok && segs.next(t, kb0, kb1)) {
           int mt, nt, bt;
           tc_tile_coords(p, t, mt, nt, bt);
           const int m0 = mt * 256 + static_cast<int>(rank) * 128;
           const int nb = nt * TC_BN + static_cast<int>(rank) * 128;  // this CTA's half of B
           const int ba = p.a_batched ? bt : 0, bb = p.b_batched ? bt : 0;
-          for (int kb = 0; kb < p.k_blocks; ++kb) {
+          for (int kb = kb0; kb < kb1; ++kb) {
             if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, ctl, kDevTimeoutEmpty)) { ok = false; break; }
             uint8_t* sa = ops + stage * Cfg::kStageBytes;
             uint8_t* sb = sa + Cfg::kABytes;
@@ -282,10 +417,12 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
         uint32_t acc_phase = 0;
         bool ok = true;
         bool issued_any = false;
-        for (int t = pair; ok && t < p.tiles_total; t += npairs) {
+        PairWork segs(p, pair, npairs);
+        int t, kb0, kb1;
+        while (ok && segs.next(t, kb0, kb1)) {
           uint32_t d_tmem = 0;
-          for (int kb = 0; kb < p.k_blocks; ++kb) {
-            const int kc = kb % p.chunk_kb;
+          for (int kb = kb0; kb < kb1; ++kb) {
+            const int kc = (kb - kb0) % p.chunk_kb;
             if (kc == 0) {
               if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
               tc_fence_after();
@@ -316,7 +453,7 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
             umma_commit_2sm(smem_u32(&empty[stage]));
             umma_commit_2sm(empty_peer0 + 8u * stage);
             if (++stage == S) { stage = 0; phase ^= 1u; }
-            if (kc == p.chunk_kb - 1 || kb == p.k_blocks - 1) {
+            if (kc == p.chunk_kb - 1 || kb == kb1 - 1) {
               umma_commit_2sm(smem_u32(&acc_full[acc]));
               umma_commit_2sm(acc_full_peer0 + 8u * acc);
               if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
@@ -342,8 +479,10 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair; ok && t < p.tiles_total; t += npairs) {
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+      PairWork segs(p, pair, npairs);
+      int t, kb0, kb1;
+      while (ok && segs.next(t, kb0, kb1)) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, ctl, kDevTimeoutFull)) { ok = false; break; }
           const uint4* x = reinterpret_cast<const uint4*>(ops + stage * Cfg::kStageBytes);
           uint4* lo = reinterpret_cast<uint4*>(lo_ops + stage * Cfg::kStageBytes);
@@ -380,7 +519,7 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
   // On the normal path the epilogue consumed the last chunk's commit, which
   // covers every MMA of the pair. After an error the odd CTA waits (bounded)
   // for the drain commit before its TMEM and shared memory may go.
-  if (warp == TC_MMA_WARP && lane == 0 && rank == 1 && pair < p.tiles_total &&
+  if (warp == TC_MMA_WARP && lane == 0 && rank == 1 &&
       *reinterpret_cast<volatile int*>(p.err) != 0) {
     const uint32_t a = smem_u32(drain);
     const uint64_t t0 = globaltimer_ns();

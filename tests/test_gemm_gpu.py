@@ -273,6 +273,65 @@ def test_tcgen05_ragged_tiles(oracle, m, n, k):
     assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
 
 
+@pytest.mark.parametrize("m,n,k,tmode", [
+    (2304, 4096, 1000, "nn"),     # 144 tiles of 256x256
+    (4352, 2500, 520, "tn"),      # 170 tiles; ragged N and K
+    (3840, 1280, 4096, "nt"),     # 75 tiles: splits fall inside K chunks
+    (8192, 1024, 2048, "nn"),     # the 8-way column shard of the 8192^2 output: 128 tiles
+    (1536, 4864, 200, "tt"),      # 114 tiles, 13 k-blocks: tiles cut into three or more parts
+])
+def test_pair_kernel_split_tiles(oracle, m, n, k, tmode):
+    """Shapes whose 256x256 tiles do not fill whole rounds of CTA pairs: the
+    last tiles' k-blocks are split between pairs and summed by the tile's
+    owner. Sampled rows against the oracle, both numeric modes, bias + ReLU,
+    and a bitwise repeat."""
+    a = rng.randu((m, k), m + 11)
+    b = rng.randu((k, n), n + 12)
+    bias = rng.randn((n,), 13, 0.1)
+    rows = np.random.default_rng(m).choice(m, 96, replace=False)
+    rows.sort()
+    ref = oracle.matmul(a, b, bias=bias, epilogue=oracle.EPI_BIAS_RELU, rows=rows)
+    # Operands as given (K-major) or as transposed views of the other layout.
+    da = DeviceView.from_host(np.ascontiguousarray(a.T)).transpose() if tmode[0] == "t" else DeviceView.from_host(a)
+    db = padded(np.ascontiguousarray(b.T)).transpose() if tmode[1] == "t" else padded(b)
+    dbias = DeviceView.from_host(bias)
+    for mode, tol in ((STRICT, STRICT_TOL), (TF32, TF32_TOL)):
+        nd = node(mode, epilogue=Epilogue.BIAS_RELU, family=KernelFamily.Tcgen05)
+        out = padded(np.zeros((m, n), np.float32))
+        with BoundGemm(nd, da, db, out, dbias) as g:
+            assert g.family == "tcgen05"
+            g.replay()
+            g.quiesce_or_abort(60)
+            first = out.to_host()
+            g.replay()
+            g.replay()
+            g.quiesce_or_abort(60)
+            again = out.to_host()
+        assert np.isfinite(first).all()
+        assert rel_frob(first[rows], ref) <= tol, (m, n, k, mode.math_mode)
+        assert np.array_equal(first.view(np.uint32), again.view(np.uint32))
+
+
+def test_pair_kernel_split_tiles_nonfinite(oracle):
+    """inf/NaN inside tiles whose k-blocks are split between pairs: the exact
+    fix-up recomputes those tiles whole."""
+    m, n, k = 2304, 4096, 640
+    a = rng.randn((m, k), 21)
+    b = rng.randn((k, n), 22)
+    a[1000, 600] = np.inf
+    a[2000, 5] = np.nan
+    b[300, 4000] = -np.inf
+    rows = np.array([0, 999, 1000, 1001, 2000, 2303])
+    ref = oracle.matmul(a, b, rows=rows)
+    got, fam = run(node(STRICT, family=KernelFamily.Tcgen05), DeviceView.from_host(a), DeviceView.from_host(b))
+    assert fam == "tcgen05"
+    got = got[rows]
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref))
+    fin = np.isfinite(ref)
+    assert rel_frob(got[fin], ref[fin]) <= STRICT_TOL
+
+
 def test_output_pad_columns_untouched():
     """A ragged output tile is clipped: padding beyond N keeps its bytes."""
     a = DeviceView.from_host(rng.randn((130, 64), 1))
