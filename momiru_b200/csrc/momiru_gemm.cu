@@ -1343,6 +1343,14 @@ int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc* d, mmr_gemm_handle** out) 
   }
   h->tcp.npeers = q;
   h->sp.npeers = q;
+  // With replicas to feed and under two rounds of tiles, every tile is split
+  // stream-K style: the pairs' ranges then end at staggered points inside
+  // tiles, so tiles finish (and their stores leave over NVLink) spread across
+  // the run instead of a round's worth at once, which would stall every
+  // epilogue behind the links together. (With more tiles than that, the
+  // round-robin order keeps its L2 reuse.) The counters cover the split: the
+  // bind sized them for up to two rounds.
+  if (h->pair && q > 0 && h->tcp.tiles_total < int(h->grid.x)) h->tcp.sk_tiles = h->tcp.tiles_total;
   *out = h;
   return MMR_OK;
 }

@@ -41,6 +41,9 @@ def _worker(rank, world, port, scenario, q):
         from momiru_b200 import BoundGemm, DeviceBuffer, DeviceView, Epilogue, MatMulNode, rng
         from momiru_b200 import _abi, execution
         from momiru_b200.sharding import ReplicatedColumnGemm
+        if scenario == "replicate_split":
+            result = _replicate_split(rank, world)
+            return
         m, k, n = 1000, 512, 1536 if scenario == "replicate" else 512
         a = rng.randu((m, k), 1)
         b = rng.randu((k, n), 2)
@@ -82,6 +85,57 @@ def _worker(rank, world, port, scenario, q):
         dist.destroy_process_group()
 
 
+def _replicate_split(rank, world):
+    """4096 x 2555 output, K = 640, 3xTF32 + bias + ReLU: each rank's column
+    block has 80 tiles of 256 x 256, more than there are CTA pairs, so its
+    tiles are split by k-blocks across pairs, and the ragged last columns go
+    through the replica copy one by one. Checks: both replicas hold the same
+    bytes, sampled rows match the oracle, and the padding columns of the
+    replicas are untouched."""
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+
+    from momiru_b200 import DeviceBuffer, DeviceView, Epilogue, MatMulNode, rng
+    from momiru_b200.sharding import ReplicatedColumnGemm
+    from oracle import oracle as O
+    m, k, n, n_phys = 4096, 640, 2555, 2560
+    a = rng.randu((m, k), 31)
+    b = rng.randu((k, n), 32)
+    bias = rng.randn((n,), 33, 0.1)
+    node = MatMulNode(epilogue=Epilogue.BIAS_RELU)
+    b_phys = np.zeros((k, n_phys), np.float32)  # rows padded to 16 bytes
+    b_phys[:, :n] = b
+    A, BIAS = DeviceView.from_host(a, rank), DeviceView.from_host(bias, rank)
+    B = DeviceView.from_host(b_phys, rank).narrow(1, 0, n)
+    out_t = torch.full((m, n_phys), 7.0, dtype=torch.float32, device=f"cuda:{rank}")
+    C = DeviceView.contiguous(DeviceBuffer.from_torch(out_t), (m, n_phys)).narrow(1, 0, n)
+    g = ReplicatedColumnGemm(node, A, B, C, BIAS, stream=torch.cuda.current_stream().cuda_stream)
+    for _ in range(3):
+        g.replay()
+    g.quiesce_or_abort(30)
+    host = out_t.cpu().numpy()
+    digest = hashlib.sha256(host.tobytes()).hexdigest()
+    everyone = [None] * world
+    dist.all_gather_object(everyone, digest)
+    rows = np.random.default_rng(5).choice(m, 64, replace=False)
+    ref = O.matmul(a, b, bias=bias, epilogue=O.EPI_BIAS_RELU, rows=rows)
+    got = host[rows, :n].astype(np.float64)
+    err = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    if len(set(everyone)) != 1:
+        result = "replicas differ"
+    elif not np.all(host[:, n:] == 7.0):
+        result = "padding written"
+    elif not err <= 1e-5:
+        result = f"error {err:.3g}"
+    else:
+        result = "ok"
+    dist.barrier()  # each rank keeps its replica mapped until both have checked
+    g.close()
+    return result
+
+
 def _run(scenario):
     import multiprocessing as mp
     ctx = mp.get_context("spawn")
@@ -99,6 +153,11 @@ def _run(scenario):
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
 def test_replicated_column_shards_match_single_gpu():
     assert _run("replicate") == {0: "ok", 1: "ok"}
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_replicated_split_tiles_and_ragged_columns():
+    assert _run("replicate_split") == {0: "ok", 1: "ok"}
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
