@@ -69,13 +69,24 @@ enum {
   MMR_MATH_EXACT = 2        /* bit-exact with the reference CPU GEMM order   */
 };
 
-/* ---- fused epilogue: MatMul -> Add(bias[N] broadcast) -> Relu, expressed in
- *      the reference as a FusedStaticDataflow node (plan.rs:1080-1106) */
+/* ---- fused epilogue: MatMul -> Add(bias[N] broadcast) -> activation,
+ *      expressed in the reference as a FusedStaticDataflow node
+ *      (plan.rs:1080-1106); the activations are the reference CPU provider's
+ *      elementwise kernels (cpu.rs:2117-2168 and 2214-2222): ReLU, ReLU6,
+ *      GELU (erf, exact), GELU (tanh approximation), SiLU */
 enum {
   MMR_EPI_NONE = 0,
   MMR_EPI_BIAS = 1,
   MMR_EPI_BIAS_RELU = 2,
-  MMR_EPI_RELU = 3
+  MMR_EPI_RELU = 3,
+  MMR_EPI_RELU6 = 4,
+  MMR_EPI_BIAS_RELU6 = 5,
+  MMR_EPI_GELU_ERF = 6,
+  MMR_EPI_BIAS_GELU_ERF = 7,
+  MMR_EPI_GELU_TANH = 8,
+  MMR_EPI_BIAS_GELU_TANH = 9,
+  MMR_EPI_SILU = 10,
+  MMR_EPI_BIAS_SILU = 11
 };
 
 /* ---- kernel family (KernelFamily, plan.rs:326-431); AUTO lets bind choose */

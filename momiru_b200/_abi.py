@@ -28,6 +28,8 @@ ERR_UNSUPPORTED_FAMILY = 12
 
 MATH_STRICT_FP32, MATH_TF32, MATH_EXACT = 0, 1, 2
 EPI_NONE, EPI_BIAS, EPI_BIAS_RELU, EPI_RELU = 0, 1, 2, 3
+EPI_RELU6, EPI_BIAS_RELU6, EPI_GELU_ERF, EPI_BIAS_GELU_ERF = 4, 5, 6, 7
+EPI_GELU_TANH, EPI_BIAS_GELU_TANH, EPI_SILU, EPI_BIAS_SILU = 8, 9, 10, 11
 FAMILY_AUTO, FAMILY_TCGEN05, FAMILY_GEMV, FAMILY_SIMT = 0, 1, 2, 3
 FAMILY_NAMES = {FAMILY_AUTO: "auto", FAMILY_TCGEN05: "tcgen05", FAMILY_GEMV: "gemv", FAMILY_SIMT: "simt"}
 

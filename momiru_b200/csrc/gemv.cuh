@@ -19,6 +19,7 @@
 #include <cooperative_groups.h>
 #include <stdint.h>
 
+#include "epilogue.cuh"
 #include "ptx.cuh"
 
 namespace mmr {
@@ -213,8 +214,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
   // Cluster reduction through DSMEM: CTA `rank` finalises a 1/GV_KSPLIT slice
   // of this strip's MT x 128 outputs, summing ranks 0..7 in order.
   const int per = (MT * GV_COLS + GV_KSPLIT - 1) / GV_KSPLIT;
-  const bool add_bias = (p.epilogue == 1 || p.epilogue == 2);
-  const bool relu = (p.epilogue == 2 || p.epilogue == 3);
+  const bool add_bias = epi_has_bias(p.epilogue);
+  const int act = epi_act(p.epilogue);
   for (int j = threadIdx.x; j < per; j += GV_THREADS) {
     const int idx = rank * per + j;
     if (idx >= MT * GV_COLS) break;
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
     const int mm = idx / GV_COLS, cc = col0 + (idx - mm * GV_COLS);
     if (mm < p.m && cc < p.n) {
       if (add_bias) sum = __fadd_rn(sum, p.bias[cc]);
-      if (relu) sum = (sum != sum) ? sum : (sum > 0.0f ? sum : 0.0f);
+      sum = act_apply(act, sum);
       p.c[mm * p.c_m + cc] = sum;
     }
   }

@@ -146,7 +146,7 @@ int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
   if (!d) return fail(MMR_ERR_INVALID_ARGUMENT, "null descriptor");
   if (d->math_mode < MMR_MATH_STRICT_FP32 || d->math_mode > MMR_MATH_EXACT)
     return fail(MMR_ERR_INVALID_ARGUMENT, "unknown math mode %d", d->math_mode);
-  if (d->epilogue < MMR_EPI_NONE || d->epilogue > MMR_EPI_RELU)
+  if (d->epilogue < MMR_EPI_NONE || d->epilogue > MMR_EPI_BIAS_SILU)
     return fail(MMR_ERR_INVALID_ARGUMENT, "unknown epilogue %d", d->epilogue);
   if (d->family < MMR_FAMILY_AUTO || d->family > MMR_FAMILY_SIMT)
     return fail(MMR_ERR_INVALID_ARGUMENT, "unknown kernel family %d", d->family);
@@ -243,7 +243,7 @@ int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
   if (ranges_overlap(C, A) || ranges_overlap(C, B))
     return fail(MMR_ERR_UNSAFE_ALIASING, "output storage overlaps an input");
 
-  const bool needs_bias = d->epilogue == MMR_EPI_BIAS || d->epilogue == MMR_EPI_BIAS_RELU;
+  const bool needs_bias = mmr::epi_has_bias(d->epilogue);
   if (needs_bias) {
     const mmr_view& V = d->bias;
     if ((rc = check_view(V, "bias", d->device_ordinal))) return rc;
@@ -719,6 +719,9 @@ int32_t noalloc_setup(int dev, NoAllocDevice** out) {
 
 }  // namespace
 
+static_assert(int(mmr::EPI_LAST) == int(MMR_EPI_BIAS_SILU) && int(mmr::EPI_BIAS_GELU_ERF) == int(MMR_EPI_BIAS_GELU_ERF),
+              "device epilogue codes follow the ABI");
+
 extern "C" {
 
 const char* mmr_last_error(void) { return g_last_error.c_str(); }
@@ -757,7 +760,7 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
                 major, minor);
   // Every bound address must be device memory of this ordinal.
   const uint64_t addrs[4] = {desc->lhs.address, desc->rhs.address, desc->out.address,
-                             (desc->epilogue == MMR_EPI_BIAS || desc->epilogue == MMR_EPI_BIAS_RELU) ? desc->bias.address : 0};
+                             mmr::epi_has_bias(desc->epilogue) ? desc->bias.address : 0};
   for (uint64_t a : addrs) {
     if (!a) continue;
     cudaPointerAttributes pa;
@@ -1168,7 +1171,7 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   MMR_CUDA_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, p.device));
   if (major != 10) return fail(MMR_ERR_UNSUPPORTED_DEVICE, "device %d is not an sm_100 device", p.device);
   const uint64_t addrs[4] = {desc->lhs.address, desc->rhs.address, desc->out.address,
-                             (desc->epilogue == MMR_EPI_BIAS || desc->epilogue == MMR_EPI_BIAS_RELU) ? desc->bias.address : 0};
+                             mmr::epi_has_bias(desc->epilogue) ? desc->bias.address : 0};
   for (uint64_t a : addrs) {
     if (!a) continue;
     cudaPointerAttributes pa;
@@ -1315,7 +1318,7 @@ int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc* d, mmr_gemm_handle** out) 
   const int raxis = d->local.transpose_rhs ? R.rank - 2 : R.rank - 1;
   local.rhs.base_offset_bytes += uint64_t(c0) * uint64_t(R.strides[raxis]) * 4u;
   local.rhs.dims[raxis] = c1 - c0;
-  if (local.epilogue == MMR_EPI_BIAS || local.epilogue == MMR_EPI_BIAS_RELU) {
+  if (mmr::epi_has_bias(local.epilogue)) {
     local.bias.base_offset_bytes += uint64_t(c0) * uint64_t(local.bias.strides[0]) * 4u;
     local.bias.dims[0] = c1 - c0;
   }

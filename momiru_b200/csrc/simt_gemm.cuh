@@ -11,6 +11,8 @@
 #pragma once
 #include <stdint.h>
 
+#include "epilogue.cuh"
+
 namespace mmr {
 
 struct SimtParams {
@@ -20,7 +22,7 @@ struct SimtParams {
   const float* b; long long b_b0, b_b1, b_k, b_n;
   float* c; long long c_b0, c_b1, c_m, c_n;
   const float* bias; long long bias_n;
-  int epilogue;  // 0 none, 1 bias, 2 bias+relu, 3 relu
+  int epilogue;  // EPI_* (epilogue.cuh)
   // Replicas of C on other ranks (same element offsets), for the exact
   // recompute of a column-sharded GEMM's flagged tiles.
   int npeers;
@@ -72,8 +74,8 @@ __device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, in
     __syncthreads();
   }
 
-  const bool add_bias = (p.epilogue == 1 || p.epilogue == 2);
-  const bool relu = (p.epilogue == 2 || p.epilogue == 3);
+  const bool add_bias = epi_has_bias(p.epilogue);
+  const int act = epi_act(p.epilogue);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int gm = m0 + ty * 4 + i;
@@ -84,7 +86,7 @@ __device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, in
       if (gn >= p.n) continue;
       float x = acc[i][j];
       if (add_bias) x = __fadd_rn(x, p.bias[gn * p.bias_n]);
-      if (relu) x = (x != x) ? x : (x > 0.0f ? x : 0.0f);
+      x = act_apply(act, x);
       C[gm * p.c_m + gn * p.c_n] = x;
       for (int q = 0; q < p.npeers; ++q)
         p.peer_c[q][b0 * p.c_b0 + b1 * p.c_b1 + gm * p.c_m + gn * p.c_n] = x;

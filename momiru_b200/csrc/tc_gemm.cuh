@@ -32,6 +32,7 @@
 // path: one atomic per affected stage) and tc_nonfinite_fixup_kernel then
 // recomputes every output of a flagged tile in the reference's exact order.
 #pragma once
+#include "epilogue.cuh"
 #include "ptx.cuh"
 #include "simt_gemm.cuh"
 
@@ -48,7 +49,6 @@ constexpr int TC_SPLIT_WARPS = 6;
 constexpr int TC_GROUP_M = 16;                  // tile raster: M-tiles per group
 constexpr int kMaxPeers = 7;                    // replicas on other ranks (8 GPUs)
 
-enum : int { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU = 3 };
 
 // Per-mode tile geometry. TF32 stages 32-wide k-blocks (128-byte rows); 3xTF32
 // stages 16-wide k-blocks (64-byte rows) so that four stages of raw + split
@@ -135,6 +135,56 @@ __device__ __forceinline__ void store_box_to_peers(const TcParams& p, const uint
   }
 }
 
+// Stores one epilogue warp's 32 x 32 box of C (lane = row; v[i] = column i,
+// bias and ReLU already applied in registers): staged in `buf` with the
+// 128-byte swizzle, a non-ReLU activation applied there (so the accumulator
+// registers are never indexed dynamically), then one TMA store plus the peer
+// copies, or, at a ragged right edge (TMA writes whole 16-byte chunks), plain
+// stores of the valid columns.
+__device__ __forceinline__ void store_box(const TcParams& p, const CUtensorMap* tmC, uint8_t* buf, const float* v,
+                                          int row0, int col0, int bt, int lane, int act) {
+  if (lane == 0) bulk_wait_group_read<0>();
+  __syncwarp();
+  // 128B-swizzled row `lane`: 16-byte chunk q lives at q ^ (lane & 7).
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    float4 w4 = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    *reinterpret_cast<float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) = w4;
+  }
+  if (act >= ACT_RELU6) {
+    __syncwarp();
+    float* f = reinterpret_cast<float*>(buf);
+    for (int e = lane; e < 32 * 32; e += 32) f[e] = act_other(act, f[e]);
+  }
+  __syncwarp();
+  if ((p.n & 3) && col0 + 32 > p.n) {
+    const int row = row0 + lane;
+    if (row < p.m) {
+      const long long off = (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 w = *reinterpret_cast<const float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4));
+        const float e4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if (col0 + 4 * q + i < p.n) {
+            p.c[off + 4 * q + i] = e4[i];
+            for (int r = 0; r < p.npeers; ++r) p.peer_c[r][off + 4 * q + i] = e4[i];
+          }
+        }
+      }
+    }
+    return;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(tmC, buf, col0, row0, bt);
+    bulk_commit_group();
+  }
+  if (p.npeers) store_box_to_peers(p, buf, row0, col0, bt, lane);
+}
+
 __device__ __forceinline__ void tc_tile_coords(const TcParams& p, int t, int& mt, int& nt, int& bt) {
   const int per_batch = p.tiles_m * p.tiles_n;
   bt = t / per_batch;
@@ -216,8 +266,9 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     uint8_t* buf = cstage + warp * TC_CSTAGE_BYTES;
-    const bool add_bias = (p.epilogue == EPI_BIAS || p.epilogue == EPI_BIAS_RELU);
-    const bool relu = (p.epilogue == EPI_BIAS_RELU || p.epilogue == EPI_RELU);
+    const bool add_bias = epi_has_bias(p.epilogue);
+    const int act = epi_act(p.epilogue);
+    const bool relu = act == ACT_RELU;
     bool ok = true;
     for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
       int mt, nt, bt;
@@ -255,40 +306,11 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
         for (int i = 0; i < 32; ++i) {
           float x = v[i];
           if (add_bias) x = __fadd_rn(x, __shfl_sync(0xffffffffu, bias_lane, i));
-          if (relu) x = (x != x) ? x : (x > 0.0f ? x : 0.0f);
+          if (relu) x = act_relu(x);
           v[i] = x;
         }
         if (row0 >= p.m || col0 >= p.n) continue;  // wholly outside C (warp-uniform)
-        if ((p.n & 3) && col0 + 32 > p.n) {
-          // Ragged right edge: TMA writes whole 16-byte chunks, so store the
-          // valid columns one by one instead.
-          const int row = row0 + lane;
-          if (row < p.m) {
-            const long long off = (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < p.n) p.c[off + i] = v[i];
-            for (int q = 0; q < p.npeers; ++q)
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < p.n) p.peer_c[q][off + i] = v[i];
-          }
-          continue;
-        }
-        if (lane == 0) bulk_wait_group_read<0>();
-        __syncwarp();
-        // 128B-swizzled row `lane`: 16-byte chunk q lives at q ^ (lane & 7).
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 w4 = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          *reinterpret_cast<float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) = w4;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&tmC, buf, col0, row0, bt);
-          bulk_commit_group();
-        }
-        if (p.npeers) store_box_to_peers(p, buf, row0, col0, bt, lane);
+        store_box(p, &tmC, buf, v, row0, col0, bt, lane, act);
       }
     }
     if (lane == 0) bulk_wait_group_all();

@@ -193,14 +193,16 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     uint8_t* buf = cstage + warp * TC_CSTAGE_BYTES;
-    const bool add_bias = (p.epilogue == EPI_BIAS || p.epilogue == EPI_BIAS_RELU);
-    const bool relu = (p.epilogue == EPI_BIAS_RELU || p.epilogue == EPI_RELU);
+    const bool add_bias = epi_has_bias(p.epilogue);
+    const int act = epi_act(p.epilogue);
+    const bool relu = act == ACT_RELU;
     const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
     // This thread's 128 columns of its row inside a partial-sum slot.
     const int ws_off = static_cast<int>(rank) * 128 * TC_BN + (quarter * 32 + lane) * TC_BN + half * 128;
     float sum[128];
 
-    // Applies bias/ReLU to sum[] and stores this thread's part of tile t.
+    // Applies the epilogue (bias, activation) to sum[] and stores this
+    // thread's part of tile t.
     auto store_tile = [&](int t) {
       int mt, nt, bt;
       tc_tile_coords(p, t, mt, nt, bt);
@@ -216,37 +218,11 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
         for (int i = 0; i < 32; ++i) {
           float x = v[i];
           if (add_bias) x = __fadd_rn(x, __shfl_sync(0xffffffffu, bias_lane, i));
-          if (relu) x = (x != x) ? x : (x > 0.0f ? x : 0.0f);
+          if (relu) x = act_relu(x);
           v[i] = x;
         }
         if (row0 >= p.m || col0 >= p.n) continue;
-        if ((p.n & 3) && col0 + 32 > p.n) {
-          const int row = row0 + lane;
-          if (row < p.m) {
-            const long long off = (long long)bt * p.c_bs + (long long)row * p.c_ld + col0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < p.n) p.c[off + i] = v[i];
-            for (int q = 0; q < p.npeers; ++q)
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < p.n) p.peer_c[q][off + i] = v[i];
-          }
-          continue;
-        }
-        if (lane == 0) bulk_wait_group_read<0>();
-        __syncwarp();
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 w4 = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          *reinterpret_cast<float4*>(buf + lane * 128 + ((q ^ (lane & 7)) << 4)) = w4;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_3d(&tmC, buf, col0, row0, bt);
-          bulk_commit_group();
-        }
-        if (p.npeers) store_box_to_peers(p, buf, row0, col0, bt, lane);
+        store_box(p, &tmC, buf, v, row0, col0, bt, lane, act);
       }
     };
     auto save_partial = [&](float* slot) {

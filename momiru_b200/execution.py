@@ -48,10 +48,25 @@ _MATH_TO_ABI = {KernelMathMode.StrictFp32: _abi.MATH_STRICT_FP32, KernelMathMode
 
 
 class Epilogue(enum.IntEnum):
+    """MatMul -> optional Add(bias[N]) -> optional activation, one fused node.
+    The activations are the reference CPU provider's elementwise kernels
+    (cpu.rs:2158-2168 ReLU/ReLU6/SiLU, 2117-2129 GELU-erf, 2214-2222 GELU-tanh)."""
     NONE = _abi.EPI_NONE
     BIAS = _abi.EPI_BIAS
     BIAS_RELU = _abi.EPI_BIAS_RELU
     RELU = _abi.EPI_RELU
+    RELU6 = _abi.EPI_RELU6
+    BIAS_RELU6 = _abi.EPI_BIAS_RELU6
+    GELU_ERF = _abi.EPI_GELU_ERF
+    BIAS_GELU_ERF = _abi.EPI_BIAS_GELU_ERF
+    GELU_TANH = _abi.EPI_GELU_TANH
+    BIAS_GELU_TANH = _abi.EPI_BIAS_GELU_TANH
+    SILU = _abi.EPI_SILU
+    BIAS_SILU = _abi.EPI_BIAS_SILU
+
+    @property
+    def has_bias(self) -> bool:
+        return self in (Epilogue.BIAS, Epilogue.BIAS_RELU) or (self >= Epilogue.RELU6 and self & 1 == 1)
 
 
 class KernelFamily(enum.IntEnum):

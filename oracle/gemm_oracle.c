@@ -15,7 +15,10 @@
  *     f32 sum (no FMA, increasing p). They are bit-identical, so one
  *     restatement (oracle_gemm) serves all three; oracle_gemm_avx2_restated
  *     keeps gemm_avx2's loop structure for the CPU timing baseline.
- *   - relu_f32       src/momiru/tensor_light/execution/cpu.rs:2156-2160
+ *   - relu_f32       src/momiru/tensor_light/execution/cpu.rs:2158-2160
+ *   - relu6_f32, silu_f32 (sigmoid_value)   cpu.rs:2137-2144, 2161-2168
+ *   - gelu_erf_f32 (erfc_nonnegative_f64, horner)   cpu.rs:2031-2129
+ *   - gelu_tanh_approx_f32                  cpu.rs:2214-2222
  *   - bias add       Elementwise Add with a trailing-axis broadcast,
  *                    src/momiru/tensor_light/execution/ir.rs:261-345
  *   - batched/broadcast matmul semantics
@@ -85,23 +88,132 @@ void oracle_randn(float *out, int64_t n, uint64_t seed, float sigma) {
 
 /* ----------------------------------------------------------- epilogues -- */
 
-enum { EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU = 3 };
+/* Epilogue codes, as the C ABI's MMR_EPI_*: MatMul -> optional Add(bias[N])
+ * -> optional activation. */
+enum {
+  EPI_NONE = 0, EPI_BIAS = 1, EPI_BIAS_RELU = 2, EPI_RELU = 3,
+  EPI_RELU6 = 4, EPI_BIAS_RELU6 = 5, EPI_GELU_ERF = 6, EPI_BIAS_GELU_ERF = 7,
+  EPI_GELU_TANH = 8, EPI_BIAS_GELU_TANH = 9, EPI_SILU = 10, EPI_BIAS_SILU = 11
+};
+enum { ACT_NONE = 0, ACT_RELU = 1, ACT_RELU6 = 2, ACT_GELU_ERF = 3, ACT_GELU_TANH = 4, ACT_SILU = 5 };
 
-/* relu_f32, cpu.rs:2156-2160: NaN kept (payload too), x>0 kept, else +0. */
+static inline int epi_has_bias(int e) { return e == EPI_BIAS || e == EPI_BIAS_RELU || (e >= EPI_RELU6 && (e & 1)); }
+static inline int epi_act(int e) {
+  if (e == EPI_BIAS_RELU || e == EPI_RELU) return ACT_RELU;
+  if (e >= EPI_RELU6 && e <= EPI_BIAS_SILU) return ACT_RELU6 + (e - EPI_RELU6) / 2;
+  return ACT_NONE;
+}
+
+/* relu_f32, cpu.rs:2158-2160: NaN kept (payload too), x>0 kept, else +0. */
 static inline float relu_ref(float x) {
   if (x != x) return x;
   if (x > 0.0f) return x;
   return 0.0f;
 }
 
+/* relu6_f32, cpu.rs:2161-2163. */
+static inline float relu6_ref(float x) {
+  if (x != x) return x;
+  if (x <= 0.0f) return 0.0f;
+  if (x >= 6.0f) return 6.0f;
+  return x;
+}
+
+/* sigmoid_value, cpu.rs:2137-2144 (exp never overflows). Rust's f32::exp is
+ * the platform libm's expf, which this calls too. */
+static inline float sigmoid_ref(float x) {
+  if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+  const float e = expf(x);
+  return e / (1.0f + e);
+}
+
+/* silu_f32, cpu.rs:2166-2168. */
+static inline float silu_ref(float x) {
+  if (x == -INFINITY) return -0.0f;
+  return x * sigmoid_ref(x);
+}
+
+/* gelu_tanh_approx_f32, cpu.rs:2214-2222: f32 arithmetic, libm tanhf. */
+static inline float gelu_tanh_ref(float x) {
+  if (x == -INFINITY) return -0.0f;
+  if (x == INFINITY) return INFINITY;
+  const float cubic = x * x * x;
+  const float t = tanhf(0.7978846f * (x + 0.044715f * cubic));
+  return 0.5f * x * (1.0f + t);
+}
+
+/* erfc of a finite nonnegative f64, cpu.rs:2031-2099: the classical rational
+ * erf / erfc approximants on [0,1), [1,8), [8,27], Horner evaluation in f64
+ * (horner / horner_leading_one, cpu.rs:2031-2046), exp(-x^2) from libm. */
+static double horner_ref(double x, const double *c, int n) {
+  double r = c[0];
+  for (int i = 1; i < n; ++i) r = r * x + c[i];
+  return r;
+}
+static double horner_one_ref(double x, const double *c, int n) {
+  double r = x + c[0];
+  for (int i = 1; i < n; ++i) r = r * x + c[i];
+  return r;
+}
+static const double ERF_T[5] = {9.60497373987051638749e0, 9.00260197203842689217e1, 2.23200534594684319226e3,
+                                7.00332514112805075473e3, 5.55923013010394962768e4};
+static const double ERF_U[5] = {3.35617141647503099647e1, 5.21357949780152679795e2, 4.59432382970980127987e3,
+                                2.26290000613890934246e4, 4.92673942608635921086e4};
+static const double ERFC_P[9] = {2.46196981473530512524e-10, 5.64189564831068821977e-1, 7.46321056442269912687e0,
+                                 4.86371970985681366614e1, 1.96520832956077098242e2, 5.26445194995477358631e2,
+                                 9.34528527171957607540e2, 1.02755188689515710272e3, 5.57535335369399327526e2};
+static const double ERFC_Q[8] = {1.32281951154744992508e1, 8.67072140885989742329e1, 3.54937778887819891062e2,
+                                 9.75708501743205489753e2, 1.82390916687909736289e3, 2.24633760818710981792e3,
+                                 1.65666309194161350182e3, 5.57535340817727675546e2};
+static const double ERFC_R[6] = {5.64189583547755073984e-1, 1.27536670759978104416e0, 5.01905042251180477414e0,
+                                 6.16021097993053585195e0, 7.40974269950448939160e0, 2.97886665372100240670e0};
+static const double ERFC_S[6] = {2.26052863220117276590e0, 9.39603524938001434673e0, 1.20489539808096656605e1,
+                                 1.70814450747565897222e1, 9.60896809063285878198e0, 3.36907645100081516050e0};
+static double erfc_nonnegative_ref(double x) {
+  if (x < 1.0) return 1.0 - x * horner_ref(x * x, ERF_T, 5) / horner_one_ref(x * x, ERF_U, 5);
+  if (x > 27.0) return 0.0;
+  const double fraction = x < 8.0 ? horner_ref(x, ERFC_P, 9) / horner_one_ref(x, ERFC_Q, 8)
+                                  : horner_ref(x, ERFC_R, 6) / horner_one_ref(x, ERFC_S, 6);
+  return exp(-x * x) * fraction;
+}
+
+/* gelu_erf_value_f32, cpu.rs:2117-2129: f64 evaluation, one rounding to f32. */
+static inline float gelu_erf_ref(float x) {
+  if (x != x || x == 0.0f) return x;
+  if (x == -INFINITY) return -0.0f;
+  if (x == INFINITY) return INFINITY;
+  const double ec = erfc_nonnegative_ref(fabs((double)x) / 1.41421356237309504880);
+  const double v = x < 0.0f ? 0.5 * (double)x * ec : 0.5 * (double)x * (2.0 - ec);
+  return (float)v;
+}
+
+static inline float activation_ref(int act, float x) {
+  switch (act) {
+    case ACT_RELU: return relu_ref(x);
+    case ACT_RELU6: return relu6_ref(x);
+    case ACT_GELU_ERF: return gelu_erf_ref(x);
+    case ACT_GELU_TANH: return gelu_tanh_ref(x);
+    case ACT_SILU: return silu_ref(x);
+    default: return x;
+  }
+}
+
 void oracle_relu(float *x, int64_t n) {
   for (int64_t i = 0; i < n; ++i) x[i] = relu_ref(x[i]);
 }
 
+/* In-place activation of n values; act is the epilogue code's activation
+ * (an MMR_EPI_* value: its bias part is ignored). Returns 1 for a bad code. */
+int oracle_activation(float *x, int64_t n, int epi) {
+  if (epi < EPI_NONE || epi > EPI_BIAS_SILU) return 1;
+  const int act = epi_act(epi);
+  for (int64_t i = 0; i < n; ++i) x[i] = activation_ref(act, x[i]);
+  return 0;
+}
+
 static inline float apply_epilogue(float s, const float *bias, int64_t col, int epi) {
-  if (epi == EPI_BIAS || epi == EPI_BIAS_RELU) s = s + bias[col];
-  if (epi == EPI_BIAS_RELU || epi == EPI_RELU) s = relu_ref(s);
-  return s;
+  if (epi_has_bias(epi)) s = s + bias[col];
+  return activation_ref(epi_act(epi), s);
 }
 
 /* ------------------------------------------------------- strided GEMM -- */
@@ -192,7 +304,8 @@ int oracle_gemm(int64_t batch, int64_t m, int64_t n, int64_t k,
                 const float *bias, int epi, const int64_t *rows, int64_t nrows,
                 int nthreads) {
   if (batch < 0 || m < 0 || n < 0 || k < 0) return 1;
-  if ((epi == EPI_BIAS || epi == EPI_BIAS_RELU) && !bias && n > 0) return 2;
+  if (epi < EPI_NONE || epi > EPI_BIAS_SILU) return 3;
+  if (epi_has_bias(epi) && !bias && n > 0) return 2;
   gemm_job j = {batch, m, n, k, a, a_sb, a_sm, a_sk, b, b_sb, b_sk, b_sn,
                 c, c_sb, c_sm, c_sn, bias, epi, rows, nrows, 0, PTHREAD_MUTEX_INITIALIZER};
   pthread_mutex_init(&j.lock, NULL);

@@ -1,8 +1,9 @@
 """ctypes loader for the CPU oracle -- TEST INFRASTRUCTURE ONLY.
 
 The oracle restates the reference CPU GEMM (gemm_dot_f32 / gemm_axpy_f32 /
-gemm_avx2, src/momiru/tensor_light/execution/cpu.rs:2989-3098), relu_f32
-(cpu.rs:2156-2160) and the SplitMix64 input generators
+gemm_avx2, src/momiru/tensor_light/execution/cpu.rs:2989-3098), the epilogue
+activations relu / relu6 / silu / gelu_erf / gelu_tanh_approx (cpu.rs:2031-2168,
+2214-2222) and the SplitMix64 input generators
 (src/momiru/tensor_light/tensor.rs:1467-1500, 1809-1840) in C. Only tests/,
 __graft_entry__.smoke() and bench.py's CPU-baseline leg import this module; the
 product path never does.
@@ -20,6 +21,8 @@ _LIB_PATH = os.path.join(_HERE, "liboracle_gemm.so")
 _lib = None
 
 EPI_NONE, EPI_BIAS, EPI_BIAS_RELU, EPI_RELU = 0, 1, 2, 3
+EPI_RELU6, EPI_BIAS_RELU6, EPI_GELU_ERF, EPI_BIAS_GELU_ERF = 4, 5, 6, 7
+EPI_GELU_TANH, EPI_BIAS_GELU_TANH, EPI_SILU, EPI_BIAS_SILU = 8, 9, 10, 11
 
 _i64 = ctypes.c_int64
 _vp = ctypes.c_void_p
@@ -50,6 +53,8 @@ def lib():
         l.oracle_randn.argtypes = [_vp, _i64, ctypes.c_uint64, ctypes.c_float]
         l.oracle_splitmix64_words.argtypes = [ctypes.c_uint64, _vp, _i64]
         l.oracle_relu.argtypes = [_vp, _i64]
+        l.oracle_activation.restype = ctypes.c_int
+        l.oracle_activation.argtypes = [_vp, _i64, ctypes.c_int]
         l.oracle_selfcheck_kat.restype = ctypes.c_int
         _lib = l
     return _lib
@@ -80,6 +85,14 @@ def splitmix64_words(seed: int, n: int) -> np.ndarray:
 def relu(x: np.ndarray) -> np.ndarray:
     y = np.ascontiguousarray(x, dtype=np.float32).copy()
     lib().oracle_relu(_ptr(y), y.size)
+    return y
+
+
+def activation(x: np.ndarray, epilogue: int) -> np.ndarray:
+    """The epilogue's activation (its bias part ignored) applied elementwise."""
+    y = np.ascontiguousarray(x, dtype=np.float32).copy()
+    if lib().oracle_activation(_ptr(y), y.size, epilogue):
+        raise ValueError(f"bad epilogue code {epilogue}")
     return y
 
 

@@ -2,6 +2,7 @@
 and its bind-time contract (validation.rs:2300-2398 shape/broadcast rules,
 layout admission, aliasing, math contract, family choice) behaves as the
 reference's validator does. No GPU: mmr_gemm_validate touches no device."""
+import ctypes
 import os
 import re
 
@@ -142,6 +143,29 @@ def test_bias_contract():
     validate(n, fake((8, 4), 1), fake((4, 16), 2), fake((8, 16), 3), fake((16,), 4))
     with pytest.raises(execution.InvalidShape):
         validate(n, fake((8, 4), 1), fake((4, 16), 2), fake((8, 16), 3), fake((8,), 4))
+
+
+def test_activation_epilogues_contract():
+    """Every MMR_EPI_* code binds on every family; the odd codes from RELU6 on
+    need a bias of N, the even ones take none; codes past BIAS_SILU are refused."""
+    views = (fake((300, 64), 1), fake((64, 520), 2), fake((300, 520), 3))
+    for e in Epilogue:
+        bias = fake((520,), 4) if e.has_bias else None
+        for fam, mode, acc in ((KernelFamily.Auto, KernelMathMode.StrictFp32, AccuracyContract.StrictFp32),
+                               (KernelFamily.Simt, KernelMathMode.Exact, AccuracyContract.Exact)):
+            validate(MatMulNode(epilogue=e, family=fam, math_mode=mode, accuracy=acc), *views, bias)
+        if e.has_bias:
+            with pytest.raises(PlanError):
+                validate(MatMulNode(epilogue=e), *views, None)
+    gv = (fake((4, 4096), 1), fake((4096, 4096), 2), fake((4, 4096), 3))
+    assert validate(MatMulNode(epilogue=Epilogue.BIAS_GELU_ERF), *gv, fake((4096,), 4))["family"] == 2
+    assert [e for e in Epilogue if e.has_bias] == [Epilogue.BIAS, Epilogue.BIAS_RELU, Epilogue.BIAS_RELU6,
+                                                   Epilogue.BIAS_GELU_ERF, Epilogue.BIAS_GELU_TANH, Epilogue.BIAS_SILU]
+    lib = _abi.load()
+    d = execution._desc(MatMulNode(), *views, None, None)
+    d.epilogue = 12
+    info = _abi.MmrGemmInfo()
+    assert lib.mmr_gemm_validate(ctypes.byref(d), ctypes.byref(info)) == _abi.ERR_INVALID_ARGUMENT
 
 
 def test_math_contract_mirrors_reference():

@@ -332,6 +332,86 @@ def test_pair_kernel_split_tiles_nonfinite(oracle):
     assert rel_frob(got[fin], ref[fin]) <= STRICT_TOL
 
 
+ACTIVATIONS = [Epilogue.RELU6, Epilogue.BIAS_RELU6, Epilogue.GELU_ERF, Epilogue.BIAS_GELU_ERF,
+               Epilogue.GELU_TANH, Epilogue.BIAS_GELU_TANH, Epilogue.SILU, Epilogue.BIAS_SILU]
+
+
+def _close_ulps(got, want, ulps, pre=None):
+    """Elementwise: equal (NaN with NaN, signed zeros and infinities alike) or
+    within `ulps` f32 units in the last place of the oracle's value. With
+    `pre` (the pre-activation values) also within 2^-21 |pre|: GELU-tanh
+    computes 0.5 x (1 + tanh(..)), and for x < 0 the sum cancels, so one or two
+    ulp of difference between two tanhf implementations near -1 become that."""
+    got = np.asarray(got, np.float32)
+    want = np.asarray(want, np.float32)
+    same = (got.view(np.uint32) == want.view(np.uint32)) | (np.isnan(got) & np.isnan(want))
+    fin = np.isfinite(want) & np.isfinite(got)
+    bound = ulps * np.spacing(np.abs(want)).astype(np.float64)
+    if pre is not None:
+        bound = np.maximum(bound, 2.0 ** -21 * np.abs(np.asarray(pre, np.float64)))
+    near = fin & (np.abs(got.astype(np.float64) - want) <= bound)
+    return bool(np.all(same | near))
+
+
+@pytest.mark.parametrize("epi", ACTIVATIONS)
+def test_activation_epilogues_every_family(oracle, epi):
+    """MatMul -> [+bias] -> ReLU6 / GELU-erf / GELU-tanh / SiLU fused into each
+    kernel family. tcgen05 and GEMV within their GEMM tolerance; the exact
+    family bit-identical for ReLU6 and within 4 f32 ulp for the transcendental
+    activations (CUDA's expf / tanhf / erfc against the host libm)."""
+    has_bias = epi.has_bias
+    cases = [
+        (300, 96, 517, KernelFamily.Tcgen05),   # CTA pairs, ragged right edge
+        (100, 200, 264, KernelFamily.Tcgen05),  # one-CTA kernel (M <= 128)
+        (4, 512, 1024, KernelFamily.Gemv),
+    ]
+    for m, k, n, fam in cases:
+        a = rng.randn((m, k), 41, 0.3)
+        b = rng.randn((k, n), 42, 0.3)
+        bias = rng.randn((n,), 43, 0.5)
+        ref = oracle.matmul(a, b, bias=bias if has_bias else None, epilogue=int(epi))
+        db = DeviceView.from_host(b) if fam == KernelFamily.Gemv else padded(b)
+        modes = ((STRICT, STRICT_TOL), (TF32, TF32_TOL)) if fam == KernelFamily.Tcgen05 else ((STRICT, STRICT_TOL),)
+        for mode, tol in modes:
+            got, f = run(node(mode, epilogue=epi, family=fam), padded(a), db,
+                         DeviceView.from_host(bias) if has_bias else None)
+            assert f == fam.name.lower()
+            assert rel_frob(got, ref) <= tol, (m, n, k, mode.math_mode)
+    a = rng.randn((70, 33), 44, 0.5)
+    b = rng.randn((33, 45), 45, 0.5)
+    bias = rng.randn((45,), 46, 0.5)
+    ref = oracle.matmul(a, b, bias=bias if has_bias else None, epilogue=int(epi))
+    got, f = run(node(EXACT, epilogue=epi), DeviceView.from_host(a), DeviceView.from_host(b),
+                 DeviceView.from_host(bias) if has_bias else None)
+    assert f == "simt"
+    if epi in (Epilogue.RELU6, Epilogue.BIAS_RELU6):
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    else:
+        pre = oracle.matmul(a, b, bias=bias if has_bias else None,
+                            epilogue=oracle.EPI_BIAS if has_bias else oracle.EPI_NONE)
+        assert _close_ulps(got, ref, 4, pre if epi in (Epilogue.GELU_TANH, Epilogue.BIAS_GELU_TANH) else None)
+
+
+def test_activation_epilogue_nonfinite_inputs(oracle):
+    """A -inf in A: GELU-erf sends -inf to -0 and +inf to +inf; NaN stays NaN
+    (3xTF32 tiles with non-finite inputs are recomputed exactly)."""
+    a = rng.randn((256, 64), 47)
+    b = rng.randn((64, 256), 48)
+    a[5, 3] = -np.inf
+    a[200, 10] = np.nan
+    bias = rng.randn((256,), 49, 0.1)
+    for epi in (Epilogue.BIAS_GELU_ERF, Epilogue.BIAS_SILU, Epilogue.BIAS_GELU_TANH):
+        ref = oracle.matmul(a, b, bias=bias, epilogue=int(epi))
+        for mode in (STRICT, TF32):
+            got, _ = run(node(mode, epilogue=epi, family=KernelFamily.Tcgen05), DeviceView.from_host(a),
+                         DeviceView.from_host(b), DeviceView.from_host(bias))
+            assert np.array_equal(np.isnan(got), np.isnan(ref)), (epi, mode.math_mode)
+            assert np.array_equal(np.isinf(got), np.isinf(ref))
+            row = ref[5]
+            neg0 = (row == 0) & np.signbit(row)
+            assert neg0.any() and np.all(np.signbit(got[5][neg0]) & (got[5][neg0] == 0))
+
+
 def test_output_pad_columns_untouched():
     """A ragged output tile is clipped: padding beyond N keeps its bytes."""
     a = DeviceView.from_host(rng.randn((130, 64), 1))

@@ -41,6 +41,80 @@ def test_relu_kat(oracle):
     assert y[8] == np.inf and y[4] == np.float32(0.25)
 
 
+NEG0 = np.float32(-0.0).view(np.uint32)
+POS0 = np.float32(0.0).view(np.uint32)
+
+
+def test_gelu_tanh_kat(oracle):
+    r = _kat()["gelu_tanh"]
+    x = np.array([float(v) for v in r["input"]], np.float32)
+    y = oracle.activation(x, oracle.EPI_GELU_TANH)
+    bits = y.view(np.uint32)
+    assert bits[2] == NEG0 and bits[3] == POS0
+    assert np.isnan(y[7]) and y[8] == np.inf
+
+
+def test_gelu_erf_kat(oracle):
+    r = _kat()["gelu_erf"]
+    x = np.array([float(v) for v in r["input"]], np.float32)
+    y = oracle.activation(x, oracle.EPI_GELU_ERF)
+    assert abs(float(y[0]) + 0.00012668497) <= 1e-8
+    assert abs(float(y[5]) - 0.8413448) <= 3e-7
+    bits = y.view(np.uint32)
+    assert bits[2] == NEG0 and bits[3] == POS0
+    assert np.isnan(y[7]) and y[8] == np.inf
+
+
+def _ulps(a, b):
+    """Distance in f32 units in the last place (same-sign finite values)."""
+    ia = a.astype(np.float32).view(np.int32).astype(np.int64)
+    ib = b.astype(np.float32).view(np.int32).astype(np.int64)
+    return np.abs(ia - ib)
+
+
+def test_activations_against_independent_f64_formulas(oracle):
+    """The restated activations stay within 1-2 f32 ulp of the same formulas
+    evaluated independently in f64 (math.erf, numpy tanh / exp), over normal
+    values and the range ends; special values as the reference defines them."""
+    import math
+    x = np.concatenate([oracle.randn(20000, 7, 3.0), np.linspace(-30, 30, 2001, dtype=np.float32)]).astype(np.float32)
+    xd = x.astype(np.float64)
+    erf = np.vectorize(math.erf)
+    ref_gelu_erf = (0.5 * xd * (1.0 + erf(xd / math.sqrt(2.0)))).astype(np.float32)
+    got = oracle.activation(x, oracle.EPI_GELU_ERF)
+    ok = np.abs(xd) < 5  # beyond, 1 + erf cancels in the independent formula
+    assert _ulps(got[ok], ref_gelu_erf[ok]).max() <= 1
+    ref_tanh = (0.5 * xd * (1.0 + np.tanh(0.7978846 * (xd + 0.044715 * xd ** 3)))).astype(np.float32)
+    got = oracle.activation(x, oracle.EPI_GELU_TANH)
+    assert np.allclose(got, ref_tanh, rtol=1e-5, atol=1e-6)
+    ref_silu = (xd / (1.0 + np.exp(-xd))).astype(np.float32)
+    got = oracle.activation(x, oracle.EPI_SILU)
+    assert np.allclose(got, ref_silu, rtol=1e-5, atol=1e-30)
+    got = oracle.activation(x, oracle.EPI_RELU6)
+    assert np.array_equal(got, np.clip(x, 0, 6).astype(np.float32))
+    sp = np.array([-np.inf, np.inf, -0.0, np.nan, 6.0, 7.5, -40.0], np.float32)
+    r6 = oracle.activation(sp, oracle.EPI_RELU6)
+    assert list(r6[[0, 1, 4, 5]]) == [0.0, 6.0, 6.0, 6.0] and r6.view(np.uint32)[2] == POS0 and np.isnan(r6[3])
+    si = oracle.activation(sp, oracle.EPI_SILU)
+    assert si.view(np.uint32)[0] == NEG0 and si[1] == np.inf and si.view(np.uint32)[2] == NEG0 and np.isnan(si[3])
+    ge = oracle.activation(sp, oracle.EPI_GELU_ERF)
+    assert ge.view(np.uint32)[0] == NEG0 and ge[1] == np.inf and ge.view(np.uint32)[6] == NEG0
+    with pytest.raises(ValueError):
+        oracle.activation(sp, 12)
+
+
+@pytest.mark.parametrize("epi", [4, 5, 6, 7, 8, 9, 10, 11])
+def test_epilogue_activations(oracle, epi):
+    a = oracle.randn(9 * 7, 1).reshape(9, 7)
+    b = oracle.randn(7 * 6, 2).reshape(7, 6)
+    bias = oracle.randn(6, 3, 0.5)
+    c = oracle.matmul(a, b)
+    pre = (c + bias).astype(np.float32) if epi & 1 else c
+    want = oracle.activation(pre, epi)
+    got = oracle.matmul(a, b, bias=bias if epi & 1 else None, epilogue=epi)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
 def test_sequential_order_is_not_reassociated(oracle):
     # 1e8 + 1 - 1e8 in increasing-p order with f32 sums gives 0, a pairwise or
     # FMA order would not: pins that every sum is a separately rounded f32 add.
