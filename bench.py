@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--mode", choices=["strict", "tf32"], default="strict")
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--panels", type=int, default=0,
+                    help="row panels of the host-buffer e2e path (0 = one per 1024 rows, at most 8)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--workload", choices=["c3", "c1", "c2", "c4", "c5a", "c5b"], default="c3",
@@ -332,6 +334,15 @@ def run_workload(args, rank, world, local):
             print(json.dumps(line), flush=True)
 
 
+def hg_panels(m, panels):
+    """Row-panel boundaries mmr_gemm_bind_host uses: whole 256-row units dealt
+    as evenly as possible; by default one panel per four units, at most 8."""
+    units = (m + 255) // 256
+    np_ = max(1, min(panels or min(8, max(1, units // 4)), max(units, 1)))
+    rows = [min(m, (i * (units // np_) + min(i, units % np_)) * 256) for i in range(np_ + 1)]
+    return list(zip(rows[:-1], rows[1:]))
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args)
@@ -422,22 +433,35 @@ def main():
     value = flops_total / (ms_step * 1e-3) / 1e12
 
     # ---------------------------------------------------------------- e2e
-    # Public API with host buffers: pinned H2D of this step's inputs, replay,
-    # D2H of the result, all inside the timed region.
+    # Public API with host buffers: this step's inputs copied in from pinned
+    # host memory, the result copied back, all inside the timed region. On one
+    # GPU that is the host-buffer entry (mmr_gemm_bind_host: rhs and bias in,
+    # then lhs by row panels overlapped with the panels' GEMMs and the copies
+    # out); across ranks each rank copies its inputs in and rank 0 copies the
+    # replicated result out.
     a_pin = torch.from_numpy(a_h).pin_memory()
     b_pin = torch.from_numpy(b_h).pin_memory()
     bias_pin = torch.from_numpy(bias_h).pin_memory()
     c_pin = torch.empty(tuple(out_t.shape), dtype=torch.float32).pin_memory() if rank == 0 else None
     h2d = (a_pin.numel() + b_pin.numel() + bias_pin.numel()) * 4
     d2h = out_t.numel() * 4
+    e2e_path = "torch copies + replicated GEMM"
+    if world == 1:
+        from momiru_b200 import HostGemm
+        hg = HostGemm(node, a_pin.numpy(), b_pin.numpy(), c_pin.numpy(), bias_pin.numpy(), panels=args.panels,
+                      device_ordinal=local, stream=stream.cuda_stream)
+        e2e_path = f"mmr_gemm_bind_host, {len(hg_panels(n, args.panels))} row panels, pinned host buffers"
 
-    def e2e_step():
-        a_t.copy_(a_pin, non_blocking=True)
-        b_t.copy_(b_pin, non_blocking=True)
-        bias_t.copy_(bias_pin, non_blocking=True)
-        g.replay()
-        if rank == 0:
-            c_pin.copy_(out_t, non_blocking=True)
+        def e2e_step():
+            hg.replay()
+    else:
+        def e2e_step():
+            a_t.copy_(a_pin, non_blocking=True)
+            b_t.copy_(b_pin, non_blocking=True)
+            bias_t.copy_(bias_pin, non_blocking=True)
+            g.replay()
+            if rank == 0:
+                c_pin.copy_(out_t, non_blocking=True)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -458,6 +482,9 @@ def main():
         dist.all_reduce(tm, op=dist.ReduceOp.MAX)
         e2e_ms = float(tm.item())
     g.quiesce_or_abort(60)
+    if world == 1:
+        hg.quiesce_or_abort(60)
+        hg.close()
     clocks.stop()
 
     # ----------------------------------------------------------- roofline
@@ -491,7 +518,7 @@ def main():
                                     + (" / 3 (3xTF32)" if args.mode == "strict" else "")),
                      "kernel_ms": kern_ms, "frac_of_tf32_peak": achieved / tf32_peak},
         "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "path": e2e_path},
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

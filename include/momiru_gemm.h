@@ -259,6 +259,24 @@ typedef struct mmr_sharded_desc {
 
 MMR_API int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc *desc, mmr_gemm_handle **out);
 
+/* ---- operands in host memory. The reference's CPU provider binds host
+ * buffers only (cpu.rs:651-654), so its callers hold their matrices in host
+ * memory; this binds the same node over HOST views (`address` = host
+ * pointer) on device `device_ordinal`. Each run copies rhs and bias in,
+ * then lhs by row panels (`panels` of them, multiples of 256 rows; 0 = one
+ * per 1024 rows, at most 8),
+ * runs the bound device GEMM of each panel as soon as its rows have landed
+ * and copies its output rows back while later panels still copy in and
+ * compute: three streams chained by events, ordered after earlier work on
+ * `desc->stream` and before later work on it. Only the logical columns are
+ * copied, so padding in host rows is never written. Host buffers should be
+ * pinned (cudaHostAlloc / cudaHostRegister) for the copies to overlap.
+ * Operands: rank 2, row-major with unit column stride; transpose_lhs = 0
+ * (lhs is streamed by rows; transpose_rhs is allowed). Device buffers are
+ * allocated here (16-byte row pitch), and the returned handle runs, waits
+ * and is freed with mmr_gemm_run / mmr_gemm_quiesce / mmr_gemm_destroy. */
+MMR_API int32_t mmr_gemm_bind_host(const mmr_matmul_desc *host_desc, int32_t panels, mmr_gemm_handle **out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,12 +4,14 @@ The compute path is the in-tree CUDA library (csrc/, built by build.py) behind
 the C ABI in include/momiru_gemm.h; this package is the host-side mirror of
 the reference's node / bind / replay / quiesce interface.
 """
-from .execution import (AccuracyContract, BoundGemm, Epilogue, GpuGemmBackend, KernelFamily, KernelMathMode,
-                        MatMulNode, PlanError, matmul, output_dims, selftest_bounded_wait, shard_columns, validate)
+from .execution import (AccuracyContract, BoundGemm, Epilogue, GpuGemmBackend, HostGemm, KernelFamily,
+                        KernelMathMode, MatMulNode, PlanError, matmul, output_dims, selftest_bounded_wait,
+                        shard_columns, validate)
 from .tensor import DeviceBuffer, DeviceView
 
 __all__ = [
-    "AccuracyContract", "BoundGemm", "DeviceBuffer", "DeviceView", "Epilogue", "GpuGemmBackend", "KernelFamily",
+    "AccuracyContract", "BoundGemm", "DeviceBuffer", "DeviceView", "Epilogue", "GpuGemmBackend", "HostGemm",
+    "KernelFamily",
     "KernelMathMode", "MatMulNode", "PlanError", "matmul", "output_dims", "selftest_bounded_wait", "shard_columns",
     "validate",
 ]

@@ -37,7 +37,7 @@ EXPORTED = [
     "mmr_gemm_validate", "mmr_gemm_bind", "mmr_gemm_run", "mmr_gemm_run_on", "mmr_gemm_quiesce",
     "mmr_gemm_destroy", "mmr_gemm_query", "mmr_last_error", "mmr_version",
     "mmr_selftest_bounded_wait", "mmr_shard_columns", "mmr_gemm_run_noalloc",
-    "mmr_ipc_export", "mmr_ipc_import", "mmr_ipc_release", "mmr_sharded_gemm_bind",
+    "mmr_ipc_export", "mmr_ipc_import", "mmr_ipc_release", "mmr_sharded_gemm_bind", "mmr_gemm_bind_host",
 ]
 NOALLOC_SCRATCH_BYTES = 64 * 1024
 NOALLOC_MAX_TILES = 8189
@@ -145,6 +145,7 @@ def load() -> ctypes.CDLL:
     lib.mmr_ipc_import.argtypes = [P(MmrIpcHandle), ctypes.c_int32, P(ctypes.c_uint64)]
     lib.mmr_ipc_release.argtypes = [ctypes.c_uint64, P(MmrIpcHandle)]
     lib.mmr_sharded_gemm_bind.argtypes = [P(MmrShardedDesc), P(h)]
+    lib.mmr_gemm_bind_host.argtypes = [P(MmrMatmulDesc), ctypes.c_int32, P(h)]
     lib.mmr_shard_columns.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       P(ctypes.c_int64), P(ctypes.c_int64)]
     for name in EXPORTED:

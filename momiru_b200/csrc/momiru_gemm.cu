@@ -17,6 +17,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <vector>
 
 #include "../../include/momiru_gemm.h"
 #include "gemv.cuh"
@@ -436,6 +437,23 @@ struct mmr_gemm_handle {
   cudaEvent_t done = nullptr, err_ev = nullptr;
   bool ran = false;
   uint64_t wait_timeout_ns = 2000000000ull;
+  // operands in host memory (mmr_gemm_bind_host): a device GEMM per row panel
+  struct Copy2D {
+    char* host = nullptr;
+    size_t host_pitch = 0;
+    char* dev = nullptr;
+    size_t dev_pitch = 0;
+    size_t width = 0;  // bytes of one row's logical columns
+    size_t rows = 0;
+  };
+  bool host = false;
+  Copy2D h_lhs, h_rhs, h_out, h_bias;
+  void* dbuf[4] = {};
+  std::vector<mmr_gemm_handle*> panel;
+  std::vector<int64_t> panel_row;  // panel i covers rows [panel_row[i], panel_row[i + 1])
+  cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_rhs = nullptr;
+  std::vector<cudaEvent_t> ev_lhs, ev_gemm;
 };
 
 namespace {
@@ -983,11 +1001,53 @@ __global__ void replica_signal_wait_kernel(const SignalParams s) {
 }
 }  // namespace
 
+// One run of a host-buffer GEMM: rhs and bias in, then per row panel: lhs
+// rows in (copy stream) -> the panel's GEMM (compute stream) -> its output rows
+// out (copy-out stream). Copies in and out run in the two PCIe directions at
+// once, under the GEMMs of other panels.
+static int32_t run_host_pipeline(mmr_gemm_handle* h, cudaStream_t s) {
+  using C2 = mmr_gemm_handle::Copy2D;
+  auto in = [&](const C2& c, size_t r0, size_t rows) -> cudaError_t {
+    if (!rows || !c.width) return cudaSuccess;
+    return cudaMemcpy2DAsync(c.dev + r0 * c.dev_pitch, c.dev_pitch, c.host + r0 * c.host_pitch, c.host_pitch, c.width,
+                             rows, cudaMemcpyHostToDevice, h->s_in);
+  };
+  MMR_CUDA_TRY(cudaEventRecord(h->ev_start, s));
+  for (cudaStream_t st : {h->s_in, h->s_comp, h->s_out}) MMR_CUDA_TRY(cudaStreamWaitEvent(st, h->ev_start, 0));
+  MMR_CUDA_TRY(in(h->h_rhs, 0, h->h_rhs.rows));
+  MMR_CUDA_TRY(in(h->h_bias, 0, h->h_bias.rows));
+  MMR_CUDA_TRY(cudaEventRecord(h->ev_rhs, h->s_in));
+  const size_t np = h->panel.size();
+  for (size_t i = 0; i < np; ++i) {
+    MMR_CUDA_TRY(in(h->h_lhs, size_t(h->panel_row[i]), size_t(h->panel_row[i + 1] - h->panel_row[i])));
+    MMR_CUDA_TRY(cudaEventRecord(h->ev_lhs[i], h->s_in));
+  }
+  MMR_CUDA_TRY(cudaStreamWaitEvent(h->s_comp, h->ev_rhs, 0));
+  for (size_t i = 0; i < np; ++i) {
+    MMR_CUDA_TRY(cudaStreamWaitEvent(h->s_comp, h->ev_lhs[i], 0));
+    if (int32_t rc = mmr_gemm_run_on(h->panel[i], h->s_comp)) return rc;
+    MMR_CUDA_TRY(cudaEventRecord(h->ev_gemm[i], h->s_comp));
+  }
+  const C2& c = h->h_out;
+  for (size_t i = 0; i < np; ++i) {
+    const size_t r0 = size_t(h->panel_row[i]), rows = size_t(h->panel_row[i + 1] - h->panel_row[i]);
+    MMR_CUDA_TRY(cudaStreamWaitEvent(h->s_out, h->ev_gemm[i], 0));
+    if (rows && c.width)
+      MMR_CUDA_TRY(cudaMemcpy2DAsync(c.host + r0 * c.host_pitch, c.host_pitch, c.dev + r0 * c.dev_pitch, c.dev_pitch,
+                                     c.width, rows, cudaMemcpyDeviceToHost, h->s_out));
+  }
+  MMR_CUDA_TRY(cudaEventRecord(h->done, h->s_out));
+  MMR_CUDA_TRY(cudaStreamWaitEvent(s, h->done, 0));  // later work on the caller's stream follows
+  h->ran = true;
+  return MMR_OK;
+}
+
 int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
   if (!h) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   DeviceGuard guard(h->device);
   if (!guard.ok) return fail(MMR_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+  if (h->host) return run_host_pipeline(h, s);
   cudaError_t e = cudaSuccess;
   if (!h->plan.empty) {
     switch (h->family) {
@@ -1049,6 +1109,11 @@ int32_t mmr_gemm_quiesce(mmr_gemm_handle* h, uint64_t timeout_ns) {
   DeviceGuard guard(h->device);
   int32_t rc = poll_event(h->done, timeout_ns);
   if (rc) return rc;
+  if (h->host) {  // every copy has landed; now each panel GEMM's error word
+    for (mmr_gemm_handle* sub : h->panel)
+      if ((rc = mmr_gemm_quiesce(sub, timeout_ns))) return rc;
+    return MMR_OK;
+  }
   // Read the device error word (asynchronously, then poll: never block forever).
   MMR_CUDA_TRY(cudaMemcpyAsync(h->h_err, h->d_err, sizeof(int), cudaMemcpyDeviceToHost, h->stream));
   MMR_CUDA_TRY(cudaEventRecord(h->err_ev, h->stream));
@@ -1073,6 +1138,20 @@ int32_t mmr_gemm_destroy(mmr_gemm_handle* h) {
   {
     DeviceGuard guard(h->device);
     if (h->ran && h->done) rc = poll_event(h->done, 10000000000ull);
+    if (h->host) {
+      for (mmr_gemm_handle* sub : h->panel) {
+        const int32_t r = mmr_gemm_destroy(sub);
+        if (rc == MMR_OK) rc = r;
+      }
+      for (void* b : h->dbuf)
+        if (b) cudaFree(b);
+      for (cudaStream_t st : {h->s_in, h->s_comp, h->s_out})
+        if (st) cudaStreamDestroy(st);
+      for (cudaEvent_t ev : h->ev_lhs) cudaEventDestroy(ev);
+      for (cudaEvent_t ev : h->ev_gemm) cudaEventDestroy(ev);
+      if (h->ev_start) cudaEventDestroy(h->ev_start);
+      if (h->ev_rhs) cudaEventDestroy(h->ev_rhs);
+    }
     if (h->done) cudaEventDestroy(h->done);
     if (h->err_ev) cudaEventDestroy(h->err_ev);
     if (h->d_err) cudaFree(h->d_err);
@@ -1354,6 +1433,122 @@ int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc* d, mmr_gemm_handle** out) 
   // round-robin order keeps its L2 reuse.) The counters cover the split: the
   // bind sized them for up to two rounds.
   if (h->pair && q > 0 && h->tcp.tiles_total < int(h->grid.x)) h->tcp.sk_tiles = h->tcp.tiles_total;
+  *out = h;
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_bind_host(const mmr_matmul_desc* d, int32_t panels, mmr_gemm_handle** out) {
+  if (!d || !out) return fail(MMR_ERR_INVALID_ARGUMENT, "null descriptor or output handle");
+  *out = nullptr;
+  if (d->lhs.rank != 2 || d->rhs.rank != 2 || d->out.rank != 2)
+    return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "host-buffer GEMM takes rank-2 lhs, rhs and out");
+  if (d->transpose_lhs)
+    return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "host-buffer GEMM streams lhs by rows: transpose_lhs is not supported");
+  if (d->epilogue < MMR_EPI_NONE || d->epilogue > MMR_EPI_BIAS_SILU)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "unknown epilogue %d", d->epilogue);
+  if (panels < 0 || panels > 64) return fail(MMR_ERR_INVALID_ARGUMENT, "panels %d outside 0..64", panels);
+  const bool has_bias = mmr::epi_has_bias(d->epilogue);
+  if (has_bias && d->bias.rank != 1) return fail(MMR_ERR_INVALID_SHAPE, "bias must be rank 1");
+  // Host views: row-major, unit column stride, inside their buffers, not device memory.
+  auto check_host = [&](const mmr_view& v, const char* name) -> int32_t {
+    const int64_t rows = v.rank == 2 ? v.dims[0] : 1, cols = v.dims[v.rank - 1];
+    const int64_t pitch = v.rank == 2 ? v.strides[0] : cols;
+    if (rows < 0 || cols < 0 || v.strides[v.rank - 1] != 1 || (v.rank == 2 && rows > 1 && pitch < cols))
+      return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: host buffer must be row-major with unit column stride", name);
+    if (v.base_offset_bytes % 4) return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: base offset not f32-aligned", name);
+    const uint64_t need = rows && cols ? uint64_t((rows - 1) * pitch + cols) * 4u : 0u;
+    if (v.base_offset_bytes + need > v.bytes) return fail(MMR_ERR_INVALID_SHAPE, "%s: view exceeds its host buffer", name);
+    if (need && !v.address) return fail(MMR_ERR_INVALID_ARGUMENT, "%s: null host address", name);
+    cudaPointerAttributes a{};
+    if (need && cudaPointerGetAttributes(&a, reinterpret_cast<void*>(v.address + v.base_offset_bytes)) == cudaSuccess &&
+        a.type == cudaMemoryTypeDevice)
+      return fail(MMR_ERR_INVALID_ARGUMENT, "%s: device memory given to the host-buffer entry (use mmr_gemm_bind)", name);
+    cudaGetLastError();
+    return MMR_OK;
+  };
+  int32_t rc;
+  if ((rc = check_host(d->lhs, "lhs")) || (rc = check_host(d->rhs, "rhs")) || (rc = check_host(d->out, "out")) ||
+      (has_bias && (rc = check_host(d->bias, "bias"))))
+    return rc;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return fail(MMR_ERR_UNSUPPORTED_DEVICE, "no CUDA device is visible");
+  if (d->device_ordinal < 0 || d->device_ordinal >= ndev)
+    return fail(MMR_ERR_UNSUPPORTED_DEVICE, "device ordinal %d outside 0..%d", d->device_ordinal, ndev - 1);
+  DeviceGuard guard(d->device_ordinal);
+  if (!guard.ok) return fail(MMR_ERR_CUDA, "cudaSetDevice(%d) failed", d->device_ordinal);
+
+  mmr_gemm_handle* h = new mmr_gemm_handle();
+  h->host = true;
+  h->device = d->device_ordinal;
+  h->stream = reinterpret_cast<cudaStream_t>(d->stream);
+  auto cleanup = [&](int32_t code) {
+    const std::string msg = mmr_last_error();
+    mmr_gemm_destroy(h);
+    return fail(code, "%s", msg.c_str());
+  };
+  // Device copies with 16-byte rows (whatever the host pitch).
+  mmr_matmul_desc dd = *d;
+  auto stage = [&](const mmr_view& v, mmr_gemm_handle::Copy2D& c, mmr_view& dv, int slot) -> int32_t {
+    const int64_t rows = v.rank == 2 ? v.dims[0] : 1, cols = v.dims[v.rank - 1];
+    const int64_t pitch = v.rank == 2 ? v.strides[0] : cols;
+    const int64_t dpitch = std::max<int64_t>((cols + 3) / 4 * 4, 4);
+    const size_t bytes = size_t(std::max<int64_t>(rows, 1)) * size_t(dpitch) * 4u;
+    if (cudaMalloc(&h->dbuf[slot], bytes) != cudaSuccess)
+      return fail(MMR_ERR_CUDA, "cudaMalloc(%zu) for a host-buffer operand failed", bytes);
+    c.host = reinterpret_cast<char*>(v.address + v.base_offset_bytes);
+    c.host_pitch = size_t(pitch) * 4u;
+    c.dev = static_cast<char*>(h->dbuf[slot]);
+    c.dev_pitch = size_t(dpitch) * 4u;
+    c.width = size_t(cols) * 4u;
+    c.rows = size_t(rows);
+    dv = v;
+    dv.address = reinterpret_cast<uint64_t>(h->dbuf[slot]);
+    dv.base_offset_bytes = 0;
+    dv.bytes = bytes;
+    dv.device_ordinal = d->device_ordinal;
+    if (v.rank == 2) dv.strides[0] = dpitch;
+    dv.allocation_id = dv.address;
+    return MMR_OK;
+  };
+  if ((rc = stage(d->lhs, h->h_lhs, dd.lhs, 0)) || (rc = stage(d->rhs, h->h_rhs, dd.rhs, 1)) ||
+      (rc = stage(d->out, h->h_out, dd.out, 2)) || (has_bias && (rc = stage(d->bias, h->h_bias, dd.bias, 3))))
+    return cleanup(rc);
+  // The whole node, validated once (shapes, math contract, family).
+  if ((rc = mmr_gemm_validate(&dd, &h->info))) return cleanup(rc);
+  h->family = h->info.family;
+  // Row panels in whole 256-row units, dealt as evenly as possible. By
+  // default one panel per four units (1024 rows, enough tiles to fill the
+  // GPU), at most eight: the last panel's GEMM and copy-out are what the
+  // copies in cannot hide.
+  const int64_t m = d->out.dims[0];
+  const int64_t units = (m + 255) / 256;
+  const int64_t want = panels ? panels : std::min<int64_t>(8, std::max<int64_t>(1, units / 4));
+  const int64_t np = std::max<int64_t>(1, std::min<int64_t>(want, std::max<int64_t>(units, 1)));
+  for (int64_t i = 0; i <= np; ++i) {
+    const int64_t u = i * (units / np) + std::min(i, units % np);
+    h->panel_row.push_back(std::min(m, u * 256));
+  }
+  for (int64_t i = 0; i < np; ++i) {
+    const int64_t r0 = h->panel_row[i], r1 = h->panel_row[i + 1];
+    mmr_matmul_desc pd = dd;
+    pd.lhs.dims[0] = r1 - r0;
+    pd.lhs.base_offset_bytes = uint64_t(r0) * uint64_t(dd.lhs.strides[0]) * 4u;
+    pd.out.dims[0] = r1 - r0;
+    pd.out.base_offset_bytes = uint64_t(r0) * uint64_t(dd.out.strides[0]) * 4u;
+    pd.stream = nullptr;
+    mmr_gemm_handle* sub = nullptr;
+    if ((rc = mmr_gemm_bind(&pd, &sub))) return cleanup(rc);
+    h->panel.push_back(sub);
+  }
+  for (cudaStream_t* st : {&h->s_in, &h->s_comp, &h->s_out})
+    if (cudaStreamCreateWithFlags(st, cudaStreamNonBlocking) != cudaSuccess)
+      return cleanup(fail(MMR_ERR_CUDA, "cudaStreamCreate failed"));
+  auto make_event = [](cudaEvent_t* ev) { return cudaEventCreateWithFlags(ev, cudaEventDisableTiming) == cudaSuccess; };
+  bool ok = make_event(&h->ev_start) && make_event(&h->ev_rhs) && make_event(&h->done);
+  h->ev_lhs.assign(size_t(np), nullptr);
+  h->ev_gemm.assign(size_t(np), nullptr);
+  for (int64_t i = 0; ok && i < np; ++i) ok = make_event(&h->ev_lhs[i]) && make_event(&h->ev_gemm[i]);
+  if (!ok) return cleanup(fail(MMR_ERR_CUDA, "cudaEventCreate failed"));
   *out = h;
   return MMR_OK;
 }

@@ -220,6 +220,100 @@ class BoundGemm:
             pass
 
 
+def _host_view(arr, device_ordinal: int) -> _abi.MmrView:
+    """An MmrView over a host f32 numpy array (row-major rows, any row pitch)."""
+    import numpy as np
+    if not isinstance(arr, np.ndarray) or arr.dtype != np.float32:
+        raise InvalidArgument("host operands are float32 numpy arrays", _abi.ERR_INVALID_ARGUMENT)
+    if arr.ndim not in (1, 2) or (arr.size and arr.strides[-1] != 4):
+        raise UnsupportedLayout("host operands are rank 1-2 with unit column stride", _abi.ERR_UNSUPPORTED_LAYOUT)
+    v = _abi.MmrView()
+    v.address = arr.ctypes.data
+    v.bytes = 4 * max(arr.size, 1) if arr.ndim == 1 else 4 * (
+        ((arr.shape[0] - 1) * (arr.strides[0] // 4) + arr.shape[1]) if arr.size else 0)
+    v.base_offset_bytes = 0
+    v.rank = arr.ndim
+    v.device_ordinal = device_ordinal
+    for i, d in enumerate(arr.shape):
+        v.dims[i] = d
+        v.strides[i] = arr.strides[i] // 4 if arr.size else (arr.shape[1] if i == 0 and arr.ndim == 2 else 1)
+    v.allocation_id = 0  # host operands are copied to buffers of the handle's own
+    return v
+
+
+class HostGemm:
+    """The MatMul node over operands in HOST memory, as the reference's own
+    CPU provider is called (cpu.rs:651-654 binds host buffers only).
+
+    Binds mmr_gemm_bind_host: each replay copies rhs and bias to the device,
+    then streams lhs by row panels (``panels``; 0 = one per 1024 rows, at most
+    8), each panel's GEMM starting as soon as its
+    rows have landed and its output rows copied back while later panels copy
+    in and compute. Arrays should live in pinned memory (e.g.
+    ``torch.empty(..., pin_memory=True).numpy()``) for the copies to overlap.
+    ``out`` may be a column-narrowed view of a wider array: only its logical
+    columns are written.
+    """
+
+    def __init__(self, node: MatMulNode, lhs, rhs, out, bias=None, panels: int = 0, device_ordinal: int = 0,
+                 stream: int | None = None):
+        self._lib = _abi.load()
+        self.node = node
+        self._arrays = (lhs, rhs, out, bias)
+        d = _abi.MmrMatmulDesc()
+        d.lhs = _host_view(lhs, device_ordinal)
+        d.rhs = _host_view(rhs, device_ordinal)
+        d.out = _host_view(out, device_ordinal)
+        if bias is not None:
+            d.bias = _host_view(bias, device_ordinal)
+        d.transpose_lhs = int(node.transpose_lhs)
+        d.transpose_rhs = int(node.transpose_rhs)
+        d.math_mode = _MATH_TO_ABI[node.math_mode]
+        d.epilogue = int(node.epilogue)
+        d.family = int(node.family)
+        d.device_ordinal = device_ordinal
+        d.stream = stream or None
+        self._handle = ctypes.c_void_p()
+        _check(self._lib.mmr_gemm_bind_host(ctypes.byref(d), int(panels), ctypes.byref(self._handle)))
+        info = _abi.MmrGemmInfo()
+        _check(self._lib.mmr_gemm_query(self._handle, ctypes.byref(info)))
+        self.info = info.as_dict()
+
+    @property
+    def family(self) -> str:
+        return _abi.FAMILY_NAMES[self.info["family"]]
+
+    def replay(self, stream: int | None = None) -> None:
+        if not self._handle:
+            raise InvalidArgument("handle closed")
+        if stream is None:
+            _check(self._lib.mmr_gemm_run(self._handle))
+        else:
+            _check(self._lib.mmr_gemm_run_on(self._handle, ctypes.c_void_p(stream)))
+
+    def quiesce_or_abort(self, timeout_s: float = 60.0) -> None:
+        _check(self._lib.mmr_gemm_quiesce(self._handle, int(timeout_s * 1e9)))
+
+    def close(self) -> None:
+        if self._handle:
+            rc = self._lib.mmr_gemm_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+            _check(rc)
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            if self._handle:
+                self._lib.mmr_gemm_destroy(self._handle)
+        except Exception:
+            pass
+
+
 class GpuGemmBackend:
     """The Backend entry point for GPU MatMul nodes (runtime.rs:954-988)."""
 

@@ -168,6 +168,43 @@ def test_activation_epilogues_contract():
     assert lib.mmr_gemm_validate(ctypes.byref(d), ctypes.byref(info)) == _abi.ERR_INVALID_ARGUMENT
 
 
+def test_host_entry_checks_arguments_before_any_device_work():
+    """mmr_gemm_bind_host: host-side argument checks (rank, transpose_lhs,
+    epilogue, bias, views inside their buffers, unit column stride) come
+    before any device call."""
+    lib = _abi.load()
+
+    def desc(a, b, c, bias=None, **kw):
+        d = _abi.MmrMatmulDesc()
+        d.lhs, d.rhs, d.out = (execution._host_view(x, 0) for x in (a, b, c))
+        if bias is not None:
+            d.bias = execution._host_view(bias, 0)
+        for k, v in kw.items():
+            setattr(d, k, v)
+        return d
+
+    a, b, c = np.zeros((8, 4), np.float32), np.zeros((4, 16), np.float32), np.zeros((8, 16), np.float32)
+    h = ctypes.c_void_p()
+    bind = lambda d: lib.mmr_gemm_bind_host(ctypes.byref(d), 0, ctypes.byref(h))
+    assert bind(desc(a, b, c, transpose_lhs=1)) == _abi.ERR_UNSUPPORTED_LAYOUT
+    d = desc(a, b, c)
+    d.lhs.rank = 3
+    assert bind(d) == _abi.ERR_UNSUPPORTED_LAYOUT
+    assert bind(desc(a, b, c, epilogue=12)) == _abi.ERR_INVALID_ARGUMENT
+    assert bind(desc(a, b, c, epilogue=int(Epilogue.BIAS_SILU))) == _abi.ERR_INVALID_SHAPE  # no bias view
+    d = desc(a, b, c)
+    d.out.bytes = 4 * 100
+    assert bind(d) == _abi.ERR_INVALID_SHAPE
+    d = desc(a, b, c)
+    d.rhs.strides[1] = 2
+    assert bind(d) == _abi.ERR_UNSUPPORTED_LAYOUT
+    assert lib.mmr_gemm_bind_host(ctypes.byref(desc(a, b, c)), 65, ctypes.byref(h)) == _abi.ERR_INVALID_ARGUMENT
+    assert not h.value
+    import torch
+    if not torch.cuda.is_available():
+        assert bind(desc(a, b, c)) == _abi.ERR_UNSUPPORTED_DEVICE
+
+
 def test_math_contract_mirrors_reference():
     # validation.rs:3579-3640
     MatMulNode(math_mode=KernelMathMode.Tf32, accuracy=AccuracyContract.AllowTf32)
