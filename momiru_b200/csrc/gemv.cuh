@@ -57,6 +57,23 @@ __host__ __device__ constexpr int gemv_smem_bytes(int mt, int kslice) {
   return gemv_ring_bytes(mt) + mt * kslice * 4 + mt * GV_COLS * 4 + 2 * GV_STAGES * 8 + 1024;
 }
 
+// Packed pairs of f32 (low half = first element) and the sm_100 packed
+// fused multiply-add, d = a * b + c per element, each rounded once.
+__device__ __forceinline__ unsigned long long pack_f32x2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack_f32x2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, unsigned long long b,
+                                                        unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 template <int MT>
 __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap tmB,
                                                                   const GemvParams p) {
@@ -121,10 +138,14 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
     const bool vec = p.a_k == 1 && (p.a_m & 3) == 0 && (k_lo & 3) == 0 &&
                      (reinterpret_cast<uintptr_t>(p.a) & 15u) == 0;
     if (vec) {
+      // Consecutive lanes take consecutive rows m of A at the same k (the
+      // warp still reads whole 32-byte sectors of each row), so their
+      // transposed stores land in consecutive words: 2-way bank conflicts at
+      // MT = 16 instead of 32-way with lanes along k.
       const int q4 = p.kslice >> 2;  // kslice is a multiple of 32
 #pragma unroll 4
       for (int idx = threadIdx.x; idx < MT * q4; idx += GV_CONSUMER_WARPS * 32) {
-        const int mm = idx / q4, kk = (idx - mm * q4) * 4;
+        const int mm = idx % MT, kk = (idx / MT) * 4;
         const int gk = k_lo + kk;
         float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         if (mm < p.m) {
@@ -144,7 +165,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
     } else {
 #pragma unroll 8
       for (int idx = threadIdx.x; idx < MT * p.kslice; idx += GV_CONSUMER_WARPS * 32) {
-        const int mm = idx / p.kslice, kk = idx - mm * p.kslice;
+        const int mm = idx % MT, kk = idx / MT;  // consecutive lanes: consecutive words of As
         const int gk = k_lo + kk;
         As[kk * MT + mm] = (mm < p.m && gk < k_hi) ? p.a[mm * p.a_m + gk * p.a_k] : 0.0f;
       }
@@ -158,6 +179,13 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
 
   if (warp < GV_CONSUMER_WARPS) {
     // ---------------------------------------------------------- consumers
+    // For MT >= 2 the sums of rows m, m+1 (adjacent in the transposed A
+    // slice) share one packed f32x2 FMA: the same per-element fused
+    // multiply-add in the same order as scalar fmaf, at half the issue slots.
+    constexpr int MP = MT >= 2 ? MT / 2 : 1;
+    unsigned long long acc2[MP][4];
+#pragma unroll
+    for (int i = 0; i < MP; ++i) acc2[i][0] = acc2[i][1] = acc2[i][2] = acc2[i][3] = 0ull;
     for (int s = 0; s < nstages; ++s) {
       const int slot = s % GV_STAGES;
       const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
@@ -169,28 +197,42 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __gri
       for (int r = 0; r < 4; ++r) {
         if (k_lo + kk0 + r < k_hi) {
           const float4 bv = *reinterpret_cast<const float4*>(st + r * (GV_COLS * 4));
-          float av[MT];
-          if constexpr (MT >= 4) {
+          if constexpr (MT >= 2) {
+            const unsigned long long bd[4] = {pack_f32x2(bv.x, bv.x), pack_f32x2(bv.y, bv.y),
+                                              pack_f32x2(bv.z, bv.z), pack_f32x2(bv.w, bv.w)};
+            unsigned long long ap[MP];
+            if constexpr (MT >= 4) {
 #pragma unroll
-            for (int i = 0; i < MT; i += 4) {
-              const float4 a4 = *reinterpret_cast<const float4*>(a0 + r * MT + i);
-              av[i] = a4.x; av[i + 1] = a4.y; av[i + 2] = a4.z; av[i + 3] = a4.w;
+              for (int i = 0; i < MT; i += 4) {
+                const float4 a4 = *reinterpret_cast<const float4*>(a0 + r * MT + i);
+                ap[i / 2] = pack_f32x2(a4.x, a4.y);
+                ap[i / 2 + 1] = pack_f32x2(a4.z, a4.w);
+              }
+            } else {
+              const float2 a2 = *reinterpret_cast<const float2*>(a0 + r * MT);
+              ap[0] = pack_f32x2(a2.x, a2.y);
             }
+#pragma unroll
+            for (int i = 0; i < MP; ++i)
+#pragma unroll
+              for (int j = 0; j < 4; ++j) acc2[i][j] = fma_f32x2(ap[i], bd[j], acc2[i][j]);
           } else {
-#pragma unroll
-            for (int i = 0; i < MT; ++i) av[i] = a0[r * MT + i];
-          }
-#pragma unroll
-          for (int i = 0; i < MT; ++i) {
-            acc[i][0] = fmaf(av[i], bv.x, acc[i][0]);
-            acc[i][1] = fmaf(av[i], bv.y, acc[i][1]);
-            acc[i][2] = fmaf(av[i], bv.z, acc[i][2]);
-            acc[i][3] = fmaf(av[i], bv.w, acc[i][3]);
+            const float av = a0[r * MT];
+            acc[0][0] = fmaf(av, bv.x, acc[0][0]);
+            acc[0][1] = fmaf(av, bv.y, acc[0][1]);
+            acc[0][2] = fmaf(av, bv.z, acc[0][2]);
+            acc[0][3] = fmaf(av, bv.w, acc[0][3]);
           }
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if constexpr (MT >= 2) {
+#pragma unroll
+      for (int i = 0; i < MP; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) unpack_f32x2(acc2[i][j], acc[2 * i][j], acc[2 * i + 1][j]);
     }
   }
   __syncthreads();  // the ring is idle from here on: reuse it for partials
