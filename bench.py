@@ -455,10 +455,22 @@ def main():
         def e2e_step():
             hg.replay()
     else:
+        # Each rank's GEMM reads all of A but only its column block of B and
+        # bias, so that is what it copies in (B's block as one pitched copy);
+        # rank 0 copies the replicated result out.
+        from cuda.bindings import runtime as cudart
+        h2d = (a_pin.numel() + n * ncols + ncols) * 4
+        e2e_path = "A + this rank's B/bias column block in, replicated GEMM, rank 0 copies C out"
+
         def e2e_step():
             a_t.copy_(a_pin, non_blocking=True)
-            b_t.copy_(b_pin, non_blocking=True)
-            bias_t.copy_(bias_pin, non_blocking=True)
+            if ncols:
+                err, = cudart.cudaMemcpy2DAsync(b_t.data_ptr() + 4 * c0, 4 * n, b_pin.data_ptr() + 4 * c0, 4 * n,
+                                                4 * ncols, n, cudart.cudaMemcpyKind.cudaMemcpyHostToDevice,
+                                                stream.cuda_stream)
+                if err != cudart.cudaError_t.cudaSuccess:
+                    raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
+                bias_t[c0:c1].copy_(bias_pin[c0:c1], non_blocking=True)
             g.replay()
             if rank == 0:
                 c_pin.copy_(out_t, non_blocking=True)
