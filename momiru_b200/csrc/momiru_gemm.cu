@@ -425,8 +425,8 @@ struct mmr_gemm_handle {
   int* h_err = nullptr;  // pinned host copy of the error word
   unsigned int* d_nf = nullptr;  // 3xTF32 non-finite bookkeeping
   float* d_ws = nullptr;         // stream-K partial sums (CTA pairs)
-  unsigned int* d_ws_flag = nullptr;
-  size_t ws_flag_bytes = 0;
+  unsigned int* d_ws_count = nullptr;
+  size_t ws_count_bytes = 0;
   int sms = 148;
   // column-sharded GEMM with replicated output
   bool sharded = false;
@@ -881,13 +881,13 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
       // counter per split tile (fewer than two rounds of them) and epilogue
       // warp of each CTA.
       const size_t ws_bytes = size_t(npairs) * 2 * mmr::kSkSlotFloats * sizeof(float);
-      h->ws_flag_bytes = size_t(2 * npairs) * 2 * mmr::TC_EPI_WARPS * sizeof(unsigned int);
+      h->ws_count_bytes = size_t(2 * npairs) * 2 * mmr::TC_EPI_WARPS * sizeof(unsigned int);
       if (cudaMalloc(&h->d_ws, ws_bytes) != cudaSuccess ||
-          cudaMalloc(&h->d_ws_flag, h->ws_flag_bytes) != cudaSuccess ||
-          cudaMemset(h->d_ws_flag, 0, h->ws_flag_bytes) != cudaSuccess)
+          cudaMalloc(&h->d_ws_count, h->ws_count_bytes) != cudaSuccess ||
+          cudaMemset(h->d_ws_count, 0, h->ws_count_bytes) != cudaSuccess)
         return cleanup(fail(MMR_ERR_CUDA, "allocating the stream-K workspace failed"));
       q.ws = h->d_ws;
-      q.ws_flag = h->d_ws_flag;
+      q.ws_count = h->d_ws_count;
       // Whole rounds of tiles stay round-robin. When the tiles do not fill
       // the last round, that round is split stream-K; when it is less than
       // half full, the round before it is split too, so that no tile is cut
@@ -1123,7 +1123,7 @@ int32_t mmr_gemm_quiesce(mmr_gemm_handle* h, uint64_t timeout_ns) {
     *h->h_err = 0;
     cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
     // A run that gave up may leave stream-K arrival counts that nothing reset.
-    if (h->d_ws_flag) cudaMemsetAsync(h->d_ws_flag, 0, h->ws_flag_bytes, h->stream);
+    if (h->d_ws_count) cudaMemsetAsync(h->d_ws_count, 0, h->ws_count_bytes, h->stream);
     return fail(code == mmr::kDevTimeoutDrain || code <= mmr::kDevTimeoutXform || code == mmr::kDevTimeoutPeer
                     ? MMR_ERR_TIMEOUT
                     : MMR_ERR_DEVICE_FAULT_FLAG,
@@ -1157,7 +1157,7 @@ int32_t mmr_gemm_destroy(mmr_gemm_handle* h) {
     if (h->d_err) cudaFree(h->d_err);
     if (h->d_nf) cudaFree(h->d_nf);
     if (h->d_ws) cudaFree(h->d_ws);
-    if (h->d_ws_flag) cudaFree(h->d_ws_flag);
+    if (h->d_ws_count) cudaFree(h->d_ws_count);
     if (h->h_err) cudaFreeHost(h->h_err);
   }
   delete h;

@@ -114,7 +114,7 @@ struct TcParams {
   // Stream-K partial sums (CTA-pair kernel): two slots per pair, and arrival
   // counters per split tile and epilogue warp of each CTA (zero between launches).
   float* ws;
-  unsigned int* ws_flag;
+  unsigned int* ws_count;
   int sk_tiles;  // trailing tiles split stream-K style (0: whole tiles only)
 };
 

@@ -19,7 +19,12 @@
 // (one per epilogue warp). The warp whose part completes the count adds the
 // parts in K order with round-to-nearest adds (so the result is the same
 // whichever pair arrives last), stores the tile and resets the counter.
-// Nothing waits on another pair, so the pairs need not be co-resident.
+// Nothing waits on another pair, so the pairs need not be co-resident. Odd
+// pairs take their segments last-first (PairWork), so a tile shared by an odd
+// pair and the next even pair is finished in mid-kernel. When the output is
+// replicated to peer GPUs and there are under two rounds of tiles, the binder
+// splits every tile this way (sk_tiles = all tiles) to spread tile
+// completions, and so the NVLink stores, over the run.
 //
 // Pair protocol (rank 0 = even CTA issues every MMA of the pair):
 //   full[s]        3xTF32: local, TMA -> split warps of the same CTA.
@@ -271,7 +276,7 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
       const int q1 = sk_pair_of(p, (long long)(ts + 1) * p.k_blocks - 1, npairs);
       unsigned int last = 0;
       if (lane == 0) {
-        unsigned int* cnt = p.ws_flag + sk_counter(ts, rank, warp);
+        unsigned int* cnt = p.ws_count + sk_counter(ts, rank, warp);
         unsigned int before;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(before) : "l"(cnt) : "memory");
         last = before == static_cast<unsigned int>(q1 - q0);
