@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--size", type=int, default=8192)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--panels", type=int, default=0,
-                    help="row panels of the host-buffer e2e path (0 = one per 1024 rows, at most 8)")
+                    help="row panels of the host-buffer e2e path (0 = one per 512 rows, at most 16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--workload", choices=["c3", "c1", "c2", "c4", "c5a", "c5b"], default="c3",
@@ -336,9 +336,9 @@ def run_workload(args, rank, world, local):
 
 def hg_panels(m, panels):
     """Row-panel boundaries mmr_gemm_bind_host uses: whole 256-row units dealt
-    as evenly as possible; by default one panel per four units, at most 8."""
+    as evenly as possible; by default one panel per two units, at most 16."""
     units = (m + 255) // 256
-    np_ = max(1, min(panels or min(8, max(1, units // 4)), max(units, 1)))
+    np_ = max(1, min(panels or min(16, max(1, units // 2)), max(units, 1)))
     rows = [min(m, (i * (units // np_) + min(i, units % np_)) * 256) for i in range(np_ + 1)]
     return list(zip(rows[:-1], rows[1:]))
 

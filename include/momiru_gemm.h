@@ -264,7 +264,7 @@ MMR_API int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc *desc, mmr_gemm_han
  * memory; this binds the same node over HOST views (`address` = host
  * pointer) on device `device_ordinal`. Each run copies rhs and bias in,
  * then lhs by row panels (`panels` of them, multiples of 256 rows; 0 = one
- * per 1024 rows, at most 8),
+ * per 512 rows, at most 16),
  * runs the bound device GEMM of each panel as soon as its rows have landed
  * and copies its output rows back while later panels still copy in and
  * compute: three streams chained by events, ordered after earlier work on

@@ -1517,12 +1517,12 @@ int32_t mmr_gemm_bind_host(const mmr_matmul_desc* d, int32_t panels, mmr_gemm_ha
   if ((rc = mmr_gemm_validate(&dd, &h->info))) return cleanup(rc);
   h->family = h->info.family;
   // Row panels in whole 256-row units, dealt as evenly as possible. By
-  // default one panel per four units (1024 rows, enough tiles to fill the
-  // GPU), at most eight: the last panel's GEMM and copy-out are what the
-  // copies in cannot hide.
+  // default one panel per two units (512 rows), at most sixteen: the last
+  // panel's GEMM and copy-out are what the copies in cannot hide (8192^3:
+  // 8 / 12 / 16 panels gave 11.6 / 11.2 / 11.0 ms per run).
   const int64_t m = d->out.dims[0];
   const int64_t units = (m + 255) / 256;
-  const int64_t want = panels ? panels : std::min<int64_t>(8, std::max<int64_t>(1, units / 4));
+  const int64_t want = panels ? panels : std::min<int64_t>(16, std::max<int64_t>(1, units / 2));
   const int64_t np = std::max<int64_t>(1, std::min<int64_t>(want, std::max<int64_t>(units, 1)));
   for (int64_t i = 0; i <= np; ++i) {
     const int64_t u = i * (units / np) + std::min(i, units % np);

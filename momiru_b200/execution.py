@@ -246,8 +246,8 @@ class HostGemm:
     CPU provider is called (cpu.rs:651-654 binds host buffers only).
 
     Binds mmr_gemm_bind_host: each replay copies rhs and bias to the device,
-    then streams lhs by row panels (``panels``; 0 = one per 1024 rows, at most
-    8), each panel's GEMM starting as soon as its
+    then streams lhs by row panels (``panels``; 0 = one per 512 rows, at most
+    16), each panel's GEMM starting as soon as its
     rows have landed and its output rows copied back while later panels copy
     in and compute. Arrays should live in pinned memory (e.g.
     ``torch.empty(..., pin_memory=True).numpy()``) for the copies to overlap.
