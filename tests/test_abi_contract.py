@@ -232,3 +232,51 @@ def test_view_ops():
     s = v.slice([(1, 4, 2), None])
     assert s.dims == (2, 6) and s.strides == (12, 1) and s.offset == 6
     assert v.is_row_major_contiguous() and not t.is_row_major_contiguous()
+
+
+def _numpy_matmul_dims(lhs, rhs, tl, tr):
+    """The node's stated semantics, NumPy matmul with the transpose flags
+    applied to the matrix axes; None where NumPy refuses (or a flag is set on
+    a rank-1 operand, which the reference rejects)."""
+    if (tl and len(lhs) == 1) or (tr and len(rhs) == 1):
+        return None
+    a = np.empty(lhs, np.float32)
+    b = np.empty(rhs, np.float32)
+    if tl:
+        a = np.swapaxes(a, -1, -2)
+    if tr:
+        b = np.swapaxes(b, -1, -2)
+    try:
+        return np.matmul(a, b).shape
+    except ValueError:
+        return None
+
+
+def test_shape_contract_matches_numpy_matmul_on_random_shapes():
+    """Random ranks 1-4, extents 0-3 (0 and 1 included, so both broadcast
+    rules and empty batches occur), transpose flags: the validator accepts
+    exactly the shapes NumPy matmul accepts and only with NumPy's output dims."""
+    from hypothesis import given, settings, strategies as st
+    dims = st.lists(st.integers(0, 3), min_size=1, max_size=4)
+
+    @settings(max_examples=300, deadline=None, derandomize=True)
+    @given(dims, dims, st.booleans(), st.booleans(), st.integers(0, 2))
+    def check(lhs, rhs, tl, tr, bump):
+        want = _numpy_matmul_dims(tuple(lhs), tuple(rhs), tl, tr)
+        node = MatMulNode(transpose_lhs=tl, transpose_rhs=tr)
+        if want is None:
+            out = tuple(max(1, x) for x in lhs[:-1] + rhs[-1:])
+            with pytest.raises(PlanError):
+                validate(node, fake(lhs, 1), fake(rhs, 2), fake(out or (1,), 3))
+            return
+        if len(want) == 0 or len(want) > 4:
+            return  # scalar results and rank > 4 are outside the view ABI
+        validate(node, fake(lhs, 1), fake(rhs, 2), fake(want, 3))
+        assert execution.output_dims(node, fake(lhs, 1), fake(rhs, 2)) == tuple(want)
+        if bump:  # any other output extent is refused
+            wrong = list(want)
+            wrong[bump % len(wrong)] += 1
+            with pytest.raises(PlanError):
+                validate(node, fake(lhs, 1), fake(rhs, 2), fake(tuple(wrong), 3))
+
+    check()
