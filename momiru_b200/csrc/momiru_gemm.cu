@@ -875,7 +875,14 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     cudaError_t ce;
     if (h->pair) {
       h->smem = h->mode ? mmr::Tc2Config<1>::kSmemBytes : mmr::Tc2Config<0>::kSmemBytes;
-      const int64_t npairs = std::min<int64_t>(tiles, sms / 2);
+      // Fewer tiles than pairs and a long K: split each tile along K over
+      // several pairs, stream-K style, in parts of at least 128 k-blocks. A
+      // split tile costs on the order of 10 us per part over the unsplit
+      // one (measured: 1024^2 x 8192 in 4 parts 319 -> 145 us, but 512^3 in
+      // 4 parts of 8 k-blocks 35 -> 72 us), so short parts do not pay.
+      const int64_t split =
+          tiles < sms / 2 ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / tiles, q.k_blocks / 128)) : 1;
+      const int64_t npairs = std::min<int64_t>(tiles, sms / 2) * split;
       h->grid = dim3(unsigned(2 * npairs));
       // Stream-K workspace: two partial-sum slots per pair, and an arrival
       // counter per split tile (fewer than two rounds of them) and epilogue
@@ -893,7 +900,7 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
       // half full, the round before it is split too, so that no tile is cut
       // into more pieces than about three pairs.
       const int64_t rem = tiles % npairs;
-      q.sk_tiles = rem == 0 ? 0 : int(2 * rem >= npairs ? rem : npairs + rem);
+      q.sk_tiles = npairs > tiles ? int(tiles) : rem == 0 ? 0 : int(2 * rem >= npairs ? rem : npairs + rem);
       h->block = dim3(h->mode ? mmr::Tc2Config<1>::kThreads : mmr::Tc2Config<0>::kThreads);
       ce = tc2_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
       h->info.cluster = 2;

@@ -312,6 +312,30 @@ def test_pair_kernel_split_tiles(oracle, m, n, k, tmode):
         assert np.array_equal(first.view(np.uint32), again.view(np.uint32))
 
 
+def test_pair_kernel_small_output_long_k(oracle):
+    """512 x 1024 output (8 pair tiles) with K = 8192: fewer tiles than CTA
+    pairs, so each tile's k-blocks are split over several pairs (4 in 3xTF32,
+    2 in TF32) and summed by the last part to arrive. Full output against the
+    oracle, bias + ReLU, and a bitwise repeat."""
+    m, n, k = 512, 1024, 8192
+    a = rng.randu((m, k), 91)
+    b = rng.randu((k, n), 92)
+    bias = rng.randn((n,), 93, 0.1)
+    ref = oracle.matmul(a, b, bias=bias, epilogue=oracle.EPI_BIAS_RELU)
+    da, db, dbias = DeviceView.from_host(a), DeviceView.from_host(b), DeviceView.from_host(bias)
+    for mode, tol in ((STRICT, STRICT_TOL), (TF32, TF32_TOL)):
+        out = DeviceView.empty((m, n))
+        with BoundGemm(node(mode, epilogue=Epilogue.BIAS_RELU, family=KernelFamily.Tcgen05), da, db, out, dbias) as g:
+            g.replay()
+            g.quiesce_or_abort(60)
+            first = out.to_host()
+            g.replay()
+            g.quiesce_or_abort(60)
+            again = out.to_host()
+        assert rel_frob(first, ref) <= tol, mode.math_mode
+        assert np.array_equal(first.view(np.uint32), again.view(np.uint32))
+
+
 def test_pair_kernel_split_tiles_nonfinite(oracle):
     """inf/NaN inside tiles whose k-blocks are split between pairs: the exact
     fix-up recomputes those tiles whole."""
