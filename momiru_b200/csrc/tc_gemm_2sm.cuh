@@ -208,13 +208,15 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
 
     // Applies the epilogue (bias, activation) to sum[] and stores this
     // thread's part of tile t.
-    auto store_tile = [&](int t) {
+    // Boxes j in [j0, j1) of this thread's four 32-column boxes.
+    auto store_tile = [&](int t, int j0 = 0, int j1 = 4) {
       int mt, nt, bt;
       tc_tile_coords(p, t, mt, nt, bt);
       const int row0 = mt * 256 + static_cast<int>(rank) * 128 + quarter * 32;
       const int nbase = nt * TC_BN + half * 128;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
+        if (j < j0 || j >= j1) continue;
         const int col0 = nbase + j * 32;
         float bias_lane = 0.0f;
         if (add_bias && col0 + lane < p.n) bias_lane = __ldg(p.bias + col0 + lane);
@@ -285,20 +287,31 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
       if (!__shfl_sync(0xffffffffu, last, 0)) continue;
       // Last part in: add the parts in K order (pairs q0 .. q1) with
       // round-to-nearest adds, whichever pair finishes, and store the tile.
+      // Done in two 64-column halves so that one part's 16 loads of a half
+      // are in flight together beside the 64 live sums (all 32 loads of a
+      // part beside all 128 sums would not fit the registers, and the loads
+      // would go out a few at a time: several L2 round trips per part).
 #pragma unroll
-      for (int i = 0; i < 128; ++i) sum[i] = 0.0f;
-      for (int q = q0; q <= q1; ++q) {
-        const float* src = p.ws + (2 * q + (q == q1 ? 0 : 1)) * kSkSlotFloats + ws_off;
+      for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
-          sum[4 * i] = __fadd_rn(sum[4 * i], v.x);
-          sum[4 * i + 1] = __fadd_rn(sum[4 * i + 1], v.y);
-          sum[4 * i + 2] = __fadd_rn(sum[4 * i + 2], v.z);
-          sum[4 * i + 3] = __fadd_rn(sum[4 * i + 3], v.w);
+        for (int i = 0; i < 64; ++i) sum[hh * 64 + i] = 0.0f;
+        for (int q = q0; q <= q1; ++q) {
+          const float4* src =
+              reinterpret_cast<const float4*>(p.ws + (2 * q + (q == q1 ? 0 : 1)) * kSkSlotFloats + ws_off) + hh * 16;
+          float4 v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = __ldcg(src + i);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float* d = sum + hh * 64 + 4 * i;
+            d[0] = __fadd_rn(d[0], v[i].x);
+            d[1] = __fadd_rn(d[1], v[i].y);
+            d[2] = __fadd_rn(d[2], v[i].z);
+            d[3] = __fadd_rn(d[3], v[i].w);
+          }
         }
+        store_tile(t, 2 * hh, 2 * hh + 2);
       }
-      store_tile(t);
     }
     if (lane == 0) bulk_wait_group_all();
     if (p.npeers) __threadfence_system();  // peer stores ordered before the completion signal
