@@ -371,11 +371,19 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
       // -------------------------------------------------------- MMA issuer
       if (lane == 0) {
         constexpr uint32_t idesc = idesc_tf32(TC_BM, TC_BN, A_MN, B_MN);
-        // Descriptor geometry: see TcConfig.
+        // Descriptor geometry: see TcConfig. Descriptors are fixed offsets from
+        // two precomputed ones (the start-address field holds shared-memory
+        // addresses >> 4 and never carries), so the issuing thread does little
+        // more than issue MMAs.
         constexpr uint32_t a_layout = A_MN ? 1u : Cfg::kKmajLayout, b_layout = B_MN ? 1u : Cfg::kKmajLayout;
         constexpr uint32_t a_lbo = A_MN ? Cfg::kMnAtomBytes : 16u, a_sbo = A_MN ? 512u : Cfg::kKmajSbo;
         constexpr uint32_t b_lbo = B_MN ? Cfg::kMnAtomBytes : 16u, b_sbo = B_MN ? 512u : Cfg::kKmajSbo;
         constexpr uint32_t a_kstep = A_MN ? 1024u : 32u, b_kstep = B_MN ? 1024u : 32u;
+        const uint64_t a_desc0 = smem_desc(smem_u32(ops), a_lbo, a_sbo, a_layout);
+        const uint64_t b_desc0 = smem_desc(smem_u32(ops) + Cfg::kABytes, b_lbo, b_sbo, b_layout);
+        constexpr uint64_t kStageStep = Cfg::kStageBytes >> 4;
+        constexpr uint64_t kLoStep = (uint64_t(S) * Cfg::kStageBytes) >> 4;  // raw -> split-off low part
+        uint64_t* const ready = MODE ? split_done : full;
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
@@ -383,44 +391,41 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
         bool ok = true;
         bool issued_any = false;
         for (int t = blockIdx.x; ok && t < p.tiles_total; t += gridDim.x) {
-          uint32_t d_tmem = 0;
-          for (int kb = 0; kb < p.k_blocks; ++kb) {
-            const int kc = kb % p.chunk_kb;
-            if (kc == 0) {
-              if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
-              tc_fence_after();
-              d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
-            }
-            uint64_t* ready = MODE ? &split_done[stage] : &full[stage];
-            if (!mbar_wait(ready, phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) { ok = false; break; }
+          for (int kb = 0; kb < p.k_blocks;) {
+            // One TMEM accumulation chunk: k-blocks [kb, chunk_end).
+            const int chunk_end = min(kb + p.chunk_kb, p.k_blocks);
+            if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sa = smem_u32(ops + stage * Cfg::kStageBytes);
-            const uint32_t sb = sa + Cfg::kABytes;
-            const uint32_t sa_lo = smem_u32(lo_ops + stage * Cfg::kStageBytes);
-            const uint32_t sb_lo = sa_lo + Cfg::kABytes;
-#pragma unroll
-            for (int kk = 0; kk < Cfg::kBK / 8; ++kk) {
-              const uint64_t ad = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_layout);
-              const uint64_t bd = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_layout);
-              const uint32_t accumulate = (kc | kk) != 0;
-              if (MODE) {
-                const uint64_t ad_lo = smem_desc(sa_lo + kk * a_kstep, a_lbo, a_sbo, a_layout);
-                const uint64_t bd_lo = smem_desc(sb_lo + kk * b_kstep, b_lbo, b_sbo, b_layout);
-                // Small cross terms first, then hi*hi.
-                umma_tf32(d_tmem, ad_lo, bd, idesc, accumulate);
-                umma_tf32(d_tmem, ad, bd_lo, idesc, 1u);
-                umma_tf32(d_tmem, ad, bd, idesc, 1u);
-              } else {
-                umma_tf32(d_tmem, ad, bd, idesc, accumulate);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
+            uint32_t accumulate = 0u;
+            for (; kb < chunk_end; ++kb) {
+              if (!mbar_wait(&ready[stage], phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) {
+                ok = false;
+                break;
               }
+              tc_fence_after();
+              const uint64_t so = static_cast<uint64_t>(stage) * kStageStep;
+#pragma unroll
+              for (int kk = 0; kk < Cfg::kBK / 8; ++kk) {
+                const uint64_t ad = a_desc0 + so + kk * (a_kstep >> 4);
+                const uint64_t bd = b_desc0 + so + kk * (b_kstep >> 4);
+                if (MODE) {
+                  // Small cross terms first, then hi*hi.
+                  umma_tf32(d_tmem, ad + kLoStep, bd, idesc, accumulate);
+                  umma_tf32(d_tmem, ad, bd + kLoStep, idesc, 1u);
+                  umma_tf32(d_tmem, ad, bd, idesc, 1u);
+                } else {
+                  umma_tf32(d_tmem, ad, bd, idesc, accumulate);
+                }
+                accumulate = 1u;
+              }
+              issued_any = true;
+              umma_commit(&empty[stage]);
+              if (++stage == S) { stage = 0; phase ^= 1u; }
             }
-            issued_any = true;
-            umma_commit(&empty[stage]);
-            if (++stage == S) { stage = 0; phase ^= 1u; }
-            if (kc == p.chunk_kb - 1 || kb == p.k_blocks - 1) {
-              umma_commit(&acc_full[acc]);
-              if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-            }
+            if (!ok) break;
+            umma_commit(&acc_full[acc]);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
           }
         }
         if (issued_any) {

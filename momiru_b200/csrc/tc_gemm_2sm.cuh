@@ -398,13 +398,27 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
     } else if (warp == TC_MMA_WARP) {
       if (lane == 0 && rank == 0) {
         // ----------------------------------------------- MMA issuer (pair)
+        // The tensor core only stays busy while this one thread keeps up: a
+        // 256x256x8 pair MMA takes 128 cycles, so the per-k-block work of the
+        // issuing thread (barrier wait, fence, descriptors, commits) has to
+        // stay well below the 768 (3xTF32) or 512 (TF32) cycles of MMAs it
+        // issues. Every descriptor is therefore a fixed offset from two
+        // precomputed ones, and the chunk bookkeeping is a counter, not a
+        // division.
         constexpr uint32_t idesc = idesc_tf32(256, TC_BN, A_MN, B_MN);
         constexpr uint32_t a_layout = A_MN ? 1u : Cfg::kKmajLayout, b_layout = B_MN ? 1u : Cfg::kKmajLayout;
         constexpr uint32_t a_lbo = A_MN ? Cfg::kMnAtomBytes : 16u, a_sbo = A_MN ? 512u : Cfg::kKmajSbo;
         constexpr uint32_t b_lbo = B_MN ? Cfg::kMnAtomBytes : 16u, b_sbo = B_MN ? 512u : Cfg::kKmajSbo;
         constexpr uint32_t a_kstep = A_MN ? 1024u : 32u, b_kstep = B_MN ? 1024u : 32u;
+        // The start-address field holds shared-memory addresses >> 4 (all below
+        // 2^18 bytes, so offsets added to it never carry out of the field).
+        const uint64_t a_desc0 = smem_desc(smem_u32(ops), a_lbo, a_sbo, a_layout);
+        const uint64_t b_desc0 = smem_desc(smem_u32(ops) + Cfg::kABytes, b_lbo, b_sbo, b_layout);
+        constexpr uint64_t kStageStep = Cfg::kStageBytes >> 4;
+        constexpr uint64_t kLoStep = (uint64_t(S) * Cfg::kStageBytes) >> 4;  // raw -> split-off low part
         const uint32_t empty_peer0 = mapa_shared(smem_u32(&empty[0]), 1);
         const uint32_t acc_full_peer0 = mapa_shared(smem_u32(&acc_full[0]), 1);
+        uint64_t* const ready = MODE ? split_done : full;
         int stage = 0;
         uint32_t phase = 0;
         int acc = 0;
@@ -414,44 +428,42 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
         PairWork segs(p, pair, npairs);
         int t, kb0, kb1;
         while (ok && segs.next(t, kb0, kb1)) {
-          uint32_t d_tmem = 0;
-          for (int kb = kb0; kb < kb1; ++kb) {
-            const int kc = (kb - kb0) % p.chunk_kb;
-            if (kc == 0) {
-              if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
-              tc_fence_after();
-              d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
-            }
-            uint64_t* ready = MODE ? &split_done[stage] : &full[stage];
-            if (!mbar_wait_cluster(ready, phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) { ok = false; break; }
+          for (int kb = kb0; kb < kb1;) {
+            // One TMEM accumulation chunk: k-blocks [kb, chunk_end).
+            const int chunk_end = min(kb + p.chunk_kb, kb1);
+            if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sa = smem_u32(ops + stage * Cfg::kStageBytes);
-            const uint32_t sb = sa + Cfg::kABytes;
-            const uint32_t sa_lo = smem_u32(lo_ops + stage * Cfg::kStageBytes);
-            const uint32_t sb_lo = sa_lo + Cfg::kABytes;
-#pragma unroll
-            for (int kk = 0; kk < Cfg::kBK / 8; ++kk) {
-              const uint64_t ad = smem_desc(sa + kk * a_kstep, a_lbo, a_sbo, a_layout);
-              const uint64_t bd = smem_desc(sb + kk * b_kstep, b_lbo, b_sbo, b_layout);
-              if (MODE) {
-                const uint64_t ad_lo = smem_desc(sa_lo + kk * a_kstep, a_lbo, a_sbo, a_layout);
-                const uint64_t bd_lo = smem_desc(sb_lo + kk * b_kstep, b_lbo, b_sbo, b_layout);
-                umma_tf32_2sm(d_tmem, ad_lo, bd, idesc, (kc | kk) != 0);
-                umma_tf32_2sm(d_tmem, ad, bd_lo, idesc, 1u);
-                umma_tf32_2sm(d_tmem, ad, bd, idesc, 1u);
-              } else {
-                umma_tf32_2sm(d_tmem, ad, bd, idesc, (kc | kk) != 0);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * TC_BN);
+            uint32_t accumulate = 0u;
+            for (; kb < chunk_end; ++kb) {
+              if (!mbar_wait_cluster(&ready[stage], phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) {
+                ok = false;
+                break;
               }
+              tc_fence_after();
+              const uint64_t so = static_cast<uint64_t>(stage) * kStageStep;
+#pragma unroll
+              for (int kk = 0; kk < Cfg::kBK / 8; ++kk) {
+                const uint64_t ad = a_desc0 + so + kk * (a_kstep >> 4);
+                const uint64_t bd = b_desc0 + so + kk * (b_kstep >> 4);
+                if (MODE) {
+                  umma_tf32_2sm(d_tmem, ad + kLoStep, bd, idesc, accumulate);  // lo(A) hi(B)
+                  umma_tf32_2sm(d_tmem, ad, bd + kLoStep, idesc, 1u);          // hi(A) lo(B)
+                  umma_tf32_2sm(d_tmem, ad, bd, idesc, 1u);                    // hi(A) hi(B)
+                } else {
+                  umma_tf32_2sm(d_tmem, ad, bd, idesc, accumulate);
+                }
+                accumulate = 1u;
+              }
+              issued_any = true;
+              umma_commit_2sm(smem_u32(&empty[stage]));
+              umma_commit_2sm(empty_peer0 + 8u * stage);
+              if (++stage == S) { stage = 0; phase ^= 1u; }
             }
-            issued_any = true;
-            umma_commit_2sm(smem_u32(&empty[stage]));
-            umma_commit_2sm(empty_peer0 + 8u * stage);
-            if (++stage == S) { stage = 0; phase ^= 1u; }
-            if (kc == p.chunk_kb - 1 || kb == kb1 - 1) {
-              umma_commit_2sm(smem_u32(&acc_full[acc]));
-              umma_commit_2sm(acc_full_peer0 + 8u * acc);
-              if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
-            }
+            if (!ok) break;
+            umma_commit_2sm(smem_u32(&acc_full[acc]));
+            umma_commit_2sm(acc_full_peer0 + 8u * acc);
+            if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
           }
         }
         if (issued_any) {
