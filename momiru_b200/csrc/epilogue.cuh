@@ -13,11 +13,14 @@
 //              0.5 x (1 + tanh(0.7978846 (x + 0.044715 x^3))) in f32
 //   gelu_erf   cpu.rs:2117-2129   NaN / +-0 kept, -inf -> -0, +inf -> +inf;
 //              else 0.5 x erfc(|x|/sqrt 2) for x < 0 and
-//              0.5 x (2 - erfc(|x|/sqrt 2)) for x > 0, in f64, rounded to f32
+//              0.5 x (2 - erfc(|x|/sqrt 2)) for x > 0, in f64, rounded to f32,
+//              with erfc the reference's own rational approximation
+//              (erfc_nonnegative_f64, cpu.rs:2031-2099), restated below
 // Products and sums are written with explicit round-to-nearest intrinsics so
 // the compiler does not contract them into FMAs the reference does not use.
-// expf / tanhf / erfc are CUDA's own library functions (the reference calls
-// its platform's libm); their last-place differences are the only difference.
+// The only library calls are the ones the reference makes to its platform's
+// libm: expf (SiLU), tanhf (GELU-tanh) and the f64 exp inside erfc; CUDA's
+// versions of those may differ from the host's in the last place.
 #pragma once
 #include <cstdint>
 
@@ -49,6 +52,56 @@ __device__ __forceinline__ float sigmoid_ref(float x) {
   return __fdiv_rn(e, __fadd_rn(1.0f, e));
 }
 
+// Horner evaluation in f64 as the reference writes it (horner and
+// horner_leading_one, cpu.rs:2031-2046): r = r * x + c with the product and
+// the sum rounded separately (the reference's Rust is never contracted to an
+// FMA).
+template <int N>
+__device__ __forceinline__ double horner_rn(double x, const double (&c)[N]) {
+  double r = c[0];
+#pragma unroll
+  for (int i = 1; i < N; ++i) r = __dadd_rn(__dmul_rn(r, x), c[i]);
+  return r;
+}
+template <int N>
+__device__ __forceinline__ double horner_one_rn(double x, const double (&c)[N]) {
+  double r = __dadd_rn(x, c[0]);
+#pragma unroll
+  for (int i = 1; i < N; ++i) r = __dadd_rn(__dmul_rn(r, x), c[i]);
+  return r;
+}
+
+// erfc of a finite nonnegative f64: the reference's erfc_nonnegative_f64
+// (cpu.rs:2062-2099), the classical rational erf / erfc approximants on
+// [0, 1), [1, 8) and [8, 27] with their published coefficients (the same
+// constants as the reference, which the result depends on to the last bit),
+// 0 above 27, and exp(-x^2) from the math library.
+__device__ __noinline__ double erfc_nonnegative(double x) {
+  constexpr double T[5] = {9.60497373987051638749e0, 9.00260197203842689217e1, 2.23200534594684319226e3,
+                           7.00332514112805075473e3, 5.55923013010394962768e4};
+  constexpr double U[5] = {3.35617141647503099647e1, 5.21357949780152679795e2, 4.59432382970980127987e3,
+                           2.26290000613890934246e4, 4.92673942608635921086e4};
+  constexpr double P[9] = {2.46196981473530512524e-10, 5.64189564831068821977e-1, 7.46321056442269912687e0,
+                           4.86371970985681366614e1,   1.96520832956077098242e2,  5.26445194995477358631e2,
+                           9.34528527171957607540e2,   1.02755188689515710272e3,  5.57535335369399327526e2};
+  constexpr double Q[8] = {1.32281951154744992508e1, 8.67072140885989742329e1, 3.54937778887819891062e2,
+                           9.75708501743205489753e2, 1.82390916687909736289e3, 2.24633760818710981792e3,
+                           1.65666309194161350182e3, 5.57535340817727675546e2};
+  constexpr double R[6] = {5.64189583547755073984e-1, 1.27536670759978104416e0, 5.01905042251180477414e0,
+                           6.16021097993053585195e0,  7.40974269950448939160e0, 2.97886665372100240670e0};
+  constexpr double S[6] = {2.26052863220117276590e0, 9.39603524938001434673e0, 1.20489539808096656605e1,
+                           1.70814450747565897222e1, 9.60896809063285878198e0, 3.36907645100081516050e0};
+  if (x < 1.0) {
+    const double x2 = __dmul_rn(x, x);
+    // 1 - (x * T(x^2)) / U(x^2), left to right as the reference writes it
+    return __dsub_rn(1.0, __ddiv_rn(__dmul_rn(x, horner_rn(x2, T)), horner_one_rn(x2, U)));
+  }
+  if (x > 27.0) return 0.0;
+  const double fraction = x < 8.0 ? __ddiv_rn(horner_rn(x, P), horner_one_rn(x, Q))
+                                  : __ddiv_rn(horner_rn(x, R), horner_one_rn(x, S));
+  return __dmul_rn(exp(__dmul_rn(-x, x)), fraction);
+}
+
 // The activations other than ReLU: called out of line, once per element, from
 // epilogues that keep their accumulators in registers.
 __device__ __noinline__ float act_other(int act, float x) {
@@ -72,7 +125,7 @@ __device__ __noinline__ float act_other(int act, float x) {
       if (x == -__int_as_float(0x7f800000)) return -0.0f;
       if (x == __int_as_float(0x7f800000)) return x;
       const double xd = static_cast<double>(x);
-      const double ec = erfc(__ddiv_rn(fabs(xd), 1.4142135623730951));
+      const double ec = erfc_nonnegative(__ddiv_rn(fabs(xd), 1.4142135623730951));
       const double half_x = __dmul_rn(0.5, xd);
       return static_cast<float>(x < 0.0f ? __dmul_rn(half_x, ec) : __dmul_rn(half_x, __dsub_rn(2.0, ec)));
     }
