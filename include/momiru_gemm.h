@@ -55,7 +55,8 @@ enum {
   MMR_ERR_UNSUPPORTED_DEVICE = 6, /* ordinal mismatch / not an sm_100 device  */
   MMR_ERR_OUT_OF_BOUNDS = 7,      /* a view does not fit its bound buffer    */
   MMR_ERR_CUDA = 8,               /* a CUDA runtime/driver call failed       */
-  MMR_ERR_NCCL = 9,               /* an NCCL call failed                     */
+  MMR_ERR_PEER_ACCESS = 9,        /* a buffer could not be shared with or
+                                     mapped from another rank's process      */
   MMR_ERR_TIMEOUT = 10,           /* bounded wait expired (host or device)   */
   MMR_ERR_DEVICE_FAULT_FLAG = 11, /* a kernel reported an error word         */
   MMR_ERR_UNSUPPORTED_FAMILY = 12 /* forced kernel family cannot run this    */
@@ -206,9 +207,12 @@ MMR_API int32_t mmr_selftest_bounded_wait(int32_t device_ordinal, uint64_t limit
  * keeps the last call's contents; each call clears the parts that must start
  * at zero before its kernels run.
  *
- * `status_out` (optional, host memory the caller keeps alive until the stream
- * has passed this call's work; pinned memory keeps the copy asynchronous)
- * receives 0, or the kernel's device error code when a bounded wait expired.
+ * `status_out` (optional: NULL, or pinned host memory -- cudaHostAlloc or
+ * cudaHostRegister -- that the caller keeps alive until the stream has passed
+ * this call's work) receives 0, or the kernel's device error code when a
+ * bounded wait expired. It is written by an asynchronous device-to-host copy
+ * enqueued on desc->stream after the kernels, so it holds the status only once
+ * the stream has reached that point.
  * Returns MMR_OK when the work was enqueued. */
 #define MMR_NOALLOC_SCRATCH_BYTES (64 * 1024)
 #define MMR_NOALLOC_MAX_TILES 8189
@@ -259,6 +263,18 @@ typedef struct mmr_sharded_desc {
 
 MMR_API int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc *desc, mmr_gemm_handle **out);
 
+/* Host-only, touches no GPU: the node rank `rank` of `nranks` binds inside
+ * mmr_sharded_gemm_bind. `whole` is validated as a whole; `local` is `whole`
+ * narrowed to the rank's column block [col0, col1) (rhs columns, bias
+ * entries, out columns, as zero-copy views), and `out_offset_bytes` is where
+ * that block starts in every replica (its byte offset from the output
+ * buffer's address), which is where the rank's epilogue stores its tiles in
+ * each peer's replica. The data-plane counterpart of the AllGather the
+ * reference IR names (ir.rs:1140-1154) for a column-sharded MatMul. */
+MMR_API int32_t mmr_shard_local_desc(const mmr_matmul_desc *whole, int32_t rank, int32_t nranks,
+                                     mmr_matmul_desc *local, int64_t *col0, int64_t *col1,
+                                     uint64_t *out_offset_bytes);
+
 /* ---- operands in host memory. The reference's CPU provider binds host
  * buffers only (cpu.rs:651-654), so its callers hold their matrices in host
  * memory; this binds the same node over HOST views (`address` = host
@@ -268,7 +284,9 @@ MMR_API int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc *desc, mmr_gemm_han
  * runs the bound device GEMM of each panel as soon as its rows have landed
  * and copies its output rows back while later panels still copy in and
  * compute: three streams chained by events, ordered after earlier work on
- * `desc->stream` and before later work on it. Only the logical columns are
+ * `desc->stream` (or the stream given to mmr_gemm_run_on) and before later
+ * work on it, and after the handle's previous run whichever stream that was
+ * on (the device staging buffers belong to the handle). Only the logical columns are
  * copied, so padding in host rows is never written. Host buffers should be
  * pinned (cudaHostAlloc / cudaHostRegister) for the copies to overlap.
  * Operands: rank 2, row-major with unit column stride; transpose_lhs = 0

@@ -21,7 +21,7 @@ ERR_UNSUPPORTED_MATH = 5
 ERR_UNSUPPORTED_DEVICE = 6
 ERR_OUT_OF_BOUNDS = 7
 ERR_CUDA = 8
-ERR_NCCL = 9
+ERR_PEER_ACCESS = 9
 ERR_TIMEOUT = 10
 ERR_DEVICE_FAULT_FLAG = 11
 ERR_UNSUPPORTED_FAMILY = 12
@@ -38,6 +38,7 @@ EXPORTED = [
     "mmr_gemm_destroy", "mmr_gemm_query", "mmr_last_error", "mmr_version",
     "mmr_selftest_bounded_wait", "mmr_shard_columns", "mmr_gemm_run_noalloc",
     "mmr_ipc_export", "mmr_ipc_import", "mmr_ipc_release", "mmr_sharded_gemm_bind", "mmr_gemm_bind_host",
+    "mmr_shard_local_desc",
 ]
 NOALLOC_SCRATCH_BYTES = 64 * 1024
 NOALLOC_MAX_TILES = 8189
@@ -146,6 +147,8 @@ def load() -> ctypes.CDLL:
     lib.mmr_ipc_release.argtypes = [ctypes.c_uint64, P(MmrIpcHandle)]
     lib.mmr_sharded_gemm_bind.argtypes = [P(MmrShardedDesc), P(h)]
     lib.mmr_gemm_bind_host.argtypes = [P(MmrMatmulDesc), ctypes.c_int32, P(h)]
+    lib.mmr_shard_local_desc.argtypes = [P(MmrMatmulDesc), ctypes.c_int32, ctypes.c_int32, P(MmrMatmulDesc),
+                                         P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_uint64)]
     lib.mmr_shard_columns.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       P(ctypes.c_int64), P(ctypes.c_int64)]
     for name in EXPORTED:

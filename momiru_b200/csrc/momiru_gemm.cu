@@ -1020,7 +1020,12 @@ static int32_t run_host_pipeline(mmr_gemm_handle* h, cudaStream_t s) {
                              rows, cudaMemcpyHostToDevice, h->s_in);
   };
   MMR_CUDA_TRY(cudaEventRecord(h->ev_start, s));
-  for (cudaStream_t st : {h->s_in, h->s_comp, h->s_out}) MMR_CUDA_TRY(cudaStreamWaitEvent(st, h->ev_start, 0));
+  for (cudaStream_t st : {h->s_in, h->s_comp, h->s_out}) {
+    MMR_CUDA_TRY(cudaStreamWaitEvent(st, h->ev_start, 0));
+    // The staging buffers are the handle's own: a run on another caller
+    // stream must not overwrite them while the previous run still uses them.
+    if (h->ran) MMR_CUDA_TRY(cudaStreamWaitEvent(st, h->done, 0));
+  }
   MMR_CUDA_TRY(in(h->h_rhs, 0, h->h_rhs.rows));
   MMR_CUDA_TRY(in(h->h_bias, 0, h->h_bias.rows));
   MMR_CUDA_TRY(cudaEventRecord(h->ev_rhs, h->s_in));
@@ -1351,7 +1356,8 @@ int32_t mmr_ipc_export(uint64_t address, mmr_ipc_handle* out) {
   if (range_fn(&base, &size, static_cast<CUdeviceptr>(address)) != CUDA_SUCCESS)
     return fail(MMR_ERR_CUDA, "cuMemGetAddressRange failed for 0x%llx", (unsigned long long)address);
   cudaIpcMemHandle_t ih;
-  MMR_CUDA_TRY(cudaIpcGetMemHandle(&ih, reinterpret_cast<void*>(base)));
+  if (cudaError_t e = cudaIpcGetMemHandle(&ih, reinterpret_cast<void*>(base)))
+    return fail(MMR_ERR_PEER_ACCESS, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
   static_assert(sizeof(ih) == sizeof(out->bytes), "IPC handle size");
   memcpy(out->bytes, &ih, sizeof ih);
   out->offset = address - static_cast<uint64_t>(base);
@@ -1365,14 +1371,51 @@ int32_t mmr_ipc_import(const mmr_ipc_handle* h, int32_t device_ordinal, uint64_t
   cudaIpcMemHandle_t ih;
   memcpy(&ih, h->bytes, sizeof ih);
   void* p = nullptr;
-  MMR_CUDA_TRY(cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess));
+  if (cudaError_t e = cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess))
+    return fail(MMR_ERR_PEER_ACCESS, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
   *address_out = reinterpret_cast<uint64_t>(p) + h->offset;
   return MMR_OK;
 }
 
 int32_t mmr_ipc_release(uint64_t address, const mmr_ipc_handle* h) {
   if (!address || !h) return fail(MMR_ERR_INVALID_ARGUMENT, "null address or handle");
-  MMR_CUDA_TRY(cudaIpcCloseMemHandle(reinterpret_cast<void*>(address - h->offset)));
+  if (cudaError_t e = cudaIpcCloseMemHandle(reinterpret_cast<void*>(address - h->offset)))
+    return fail(MMR_ERR_PEER_ACCESS, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return MMR_OK;
+}
+
+int32_t mmr_shard_local_desc(const mmr_matmul_desc* whole_desc, int32_t rank, int32_t nranks,
+                             mmr_matmul_desc* local_out, int64_t* col0, int64_t* col1, uint64_t* out_offset_bytes) {
+  if (!whole_desc || !local_out || !col0 || !col1 || !out_offset_bytes)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "null descriptor or output");
+  if (nranks < 1 || nranks > 8 || rank < 0 || rank >= nranks)
+    return fail(MMR_ERR_INVALID_ARGUMENT, "rank %d of %d outside 1..8 ranks", rank, nranks);
+  // Validate the whole node first, then narrow to this rank's column block.
+  Plan whole;
+  int32_t rc = build_plan(whole_desc, &whole);
+  if (rc) return rc;
+  const mmr_view& O = whole_desc->out;
+  if (O.rank < 2 || whole_desc->rhs.rank < 2)
+    return fail(MMR_ERR_INVALID_SHAPE, "column sharding needs matrix operands (rank >= 2)");
+  int64_t c0 = 0, c1 = 0;
+  if ((rc = mmr_shard_columns(whole.n, nranks, rank, mmr::TC_BN, &c0, &c1))) return rc;
+  mmr_matmul_desc local = *whole_desc;
+  // out[..., c0:c1]
+  local.out.base_offset_bytes += uint64_t(c0) * uint64_t(O.strides[O.rank - 1]) * 4u;
+  local.out.dims[O.rank - 1] = c1 - c0;
+  // rhs[..., :, c0:c1] (columns are the rhs's last axis, or its second to last when transposed)
+  const mmr_view& R = whole_desc->rhs;
+  const int raxis = whole_desc->transpose_rhs ? R.rank - 2 : R.rank - 1;
+  local.rhs.base_offset_bytes += uint64_t(c0) * uint64_t(R.strides[raxis]) * 4u;
+  local.rhs.dims[raxis] = c1 - c0;
+  if (mmr::epi_has_bias(local.epilogue)) {
+    local.bias.base_offset_bytes += uint64_t(c0) * uint64_t(local.bias.strides[0]) * 4u;
+    local.bias.dims[0] = c1 - c0;
+  }
+  *local_out = local;
+  *col0 = c0;
+  *col1 = c1;
+  *out_offset_bytes = local.out.base_offset_bytes;
   return MMR_OK;
 }
 
@@ -1385,29 +1428,13 @@ int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc* d, mmr_gemm_handle** out) 
   for (int i = 0; i < d->nranks; ++i)
     if (i != d->rank && (!d->peer_out[i] || !d->peer_signal[i]))
       return fail(MMR_ERR_INVALID_ARGUMENT, "rank %d's replica or signal array is not mapped", i);
-  // Validate the whole node first, then narrow to this rank's column block.
-  Plan whole;
-  int32_t rc = build_plan(&d->local, &whole);
+  mmr_matmul_desc local;
+  int64_t c0 = 0, c1 = 0;
+  uint64_t out_off = 0;
+  int32_t rc = mmr_shard_local_desc(&d->local, d->rank, d->nranks, &local, &c0, &c1, &out_off);
   if (rc) return rc;
   const mmr_view& O = d->local.out;
-  if (O.rank < 2 || d->local.rhs.rank < 2)
-    return fail(MMR_ERR_INVALID_SHAPE, "column sharding needs matrix operands (rank >= 2)");
-  int64_t c0 = 0, c1 = 0;
-  if ((rc = mmr_shard_columns(whole.n, d->nranks, d->rank, mmr::TC_BN, &c0, &c1))) return rc;
-  mmr_matmul_desc local = d->local;
   local.family = MMR_FAMILY_TCGEN05;
-  // out[..., c0:c1]
-  local.out.base_offset_bytes += uint64_t(c0) * uint64_t(O.strides[O.rank - 1]) * 4u;
-  local.out.dims[O.rank - 1] = c1 - c0;
-  // rhs[..., :, c0:c1] (columns are the rhs's last axis, or its second to last when transposed)
-  const mmr_view& R = d->local.rhs;
-  const int raxis = d->local.transpose_rhs ? R.rank - 2 : R.rank - 1;
-  local.rhs.base_offset_bytes += uint64_t(c0) * uint64_t(R.strides[raxis]) * 4u;
-  local.rhs.dims[raxis] = c1 - c0;
-  if (mmr::epi_has_bias(local.epilogue)) {
-    local.bias.base_offset_bytes += uint64_t(c0) * uint64_t(local.bias.strides[0]) * 4u;
-    local.bias.dims[0] = c1 - c0;
-  }
   mmr_gemm_handle* h = nullptr;
   if (c1 > c0) {
     if ((rc = mmr_gemm_bind(&local, &h))) return rc;

@@ -94,14 +94,14 @@ class InvalidAccuracyContract(PlanError): code = _abi.ERR_UNSUPPORTED_MATH
 class UnsupportedDevice(PlanError): code = _abi.ERR_UNSUPPORTED_DEVICE
 class OutOfBounds(PlanError): code = _abi.ERR_OUT_OF_BOUNDS
 class CudaError(PlanError): code = _abi.ERR_CUDA
-class NcclError(PlanError): code = _abi.ERR_NCCL
+class PeerAccessError(PlanError): code = _abi.ERR_PEER_ACCESS
 class QuiescenceTimeout(PlanError): code = _abi.ERR_TIMEOUT
 class DeviceErrorFlag(PlanError): code = _abi.ERR_DEVICE_FAULT_FLAG
 class UnsupportedFamily(PlanError): code = _abi.ERR_UNSUPPORTED_FAMILY
 
 
 _BY_CODE = {c.code: c for c in (InvalidArgument, InvalidShape, UnsupportedLayout, UnsafeAliasing,
-                                InvalidAccuracyContract, UnsupportedDevice, OutOfBounds, CudaError, NcclError,
+                                InvalidAccuracyContract, UnsupportedDevice, OutOfBounds, CudaError, PeerAccessError,
                                 QuiescenceTimeout, DeviceErrorFlag, UnsupportedFamily)}
 
 

@@ -2,20 +2,22 @@
 
 The reference IR names the collectives a sharded node would need
 (CollectiveSpec, src/momiru/tensor_light/execution/ir.rs:1140-1154) but
-rejects AllGather today (ir.rs:1773-1779); this module is the host-side plan
-for the two partitions the GPU path uses:
+rejects AllGather today (ir.rs:1773-1779). The GPU path uses two partitions:
 
   * columns: rank r owns output columns [c0, c1) in whole 256-column tile
-    units (mmr_shard_columns); it binds the ordinary GEMM on the zero-copy
-    views B[:, c0:c1], bias[c0:c1], C[:, c0:c1]; replicating C then needs an
-    all-gather of the column blocks.
+    units (mmr_shard_columns) and binds the ordinary GEMM on the zero-copy
+    views B[:, c0:c1], bias[c0:c1], C[:, c0:c1] (mmr_shard_local_desc). When
+    the output is replicated, the GEMM's own epilogue stores every finished
+    tile into each rank's replica over NVLink (mmr_sharded_gemm_bind): the
+    all-gather is fused into the GEMM and no collective runs on the data path.
+    The only host exchange is the one-time swap of IPC handles at bind.
   * batch: rank r owns batch entries [b0, b1); no collective.
 
-The arithmetic here is plain Python so it runs (and is tested) on CPU ranks.
+The partition arithmetic is plain Python so it runs (and is tested) on CPU
+ranks; `local_shard` calls the library's host-only narrowing, the same code
+mmr_sharded_gemm_bind runs.
 """
 from __future__ import annotations
-
-from dataclasses import dataclass
 
 TILE_N = 256
 
@@ -45,36 +47,31 @@ def batch_shards(batch: int, world: int) -> list[tuple[int, int]]:
     return out
 
 
-@dataclass(frozen=True)
-class GatherLayout:
-    """Where each rank's column block lands in the gathered buffer.
+def local_shard(desc, rank: int, world: int):
+    """The node rank `rank` binds in a column-sharded run: `desc` (a whole
+    mmr_matmul_desc) narrowed to the rank's column block. Returns
+    (local_desc, c0, c1, out_offset_bytes), out_offset_bytes being where the
+    block starts in every output replica. Host only (mmr_shard_local_desc)."""
+    import ctypes
 
-    All-gather moves equal-sized blocks, so each rank's block is padded to
-    the widest shard: gathered[r] is an [m, width] block whose first
-    (c1 - c0) columns are rank r's output columns c0..c1-1."""
-    m: int
-    n: int
-    width: int
-    shards: tuple
+    from . import _abi, execution
+    lib = _abi.load()
+    local = _abi.MmrMatmulDesc()
+    c0, c1, off = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_uint64()
+    execution._check(lib.mmr_shard_local_desc(ctypes.byref(desc), rank, world, ctypes.byref(local),
+                                              ctypes.byref(c0), ctypes.byref(c1), ctypes.byref(off)))
+    return local, c0.value, c1.value, off.value
 
-    @staticmethod
-    def make(m: int, n: int, world: int, align: int = TILE_N) -> "GatherLayout":
-        shards = tuple(column_shards(n, world, align))
-        width = max(c1 - c0 for c0, c1 in shards) if shards else 0
-        return GatherLayout(m, n, max(width, 1), shards)
 
-    def assemble(self, gathered):
-        """gathered: array-like [world, m, width] (numpy or torch) -> [m, n]."""
-        import numpy as np
-        is_np = isinstance(gathered, np.ndarray)
-        if is_np:
-            out = np.empty((self.m, self.n), dtype=gathered.dtype)
-        else:
-            import torch
-            out = torch.empty((self.m, self.n), dtype=gathered.dtype, device=gathered.device)
-        for r, (c0, c1) in enumerate(self.shards):
-            out[:, c0:c1] = gathered[r][:, :c1 - c0]
-        return out
+def exchange_replica_handles(mine, group=None) -> list:
+    """Bind-time exchange: every rank contributes the IPC handles of its output
+    replica and its completion-signal array, as ((handle bytes, offset),
+    (handle bytes, offset)); every rank receives all ranks' pairs in rank order.
+    The only collective of the replicated GEMM, run once at bind."""
+    import torch.distributed as dist
+    everyone = [None] * dist.get_world_size(group)
+    dist.all_gather_object(everyone, mine, group=group)
+    return everyone
 
 
 class ReplicatedColumnGemm:
@@ -111,8 +108,7 @@ class ReplicatedColumnGemm:
             return bytes(h.bytes), int(h.offset)
 
         mine = (export(out.buffer.address), export(self._signal.data_ptr()))
-        everyone = [None] * self.world
-        dist.all_gather_object(everyone, mine)
+        everyone = exchange_replica_handles(mine)
         self._imported = []
         d = _abi.MmrShardedDesc()
         d.local = execution._desc(node, lhs, rhs, out, bias, stream)
