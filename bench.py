@@ -127,9 +127,39 @@ class ClockSampler:
                 "power_w_max": max(pw) if pw else None}
 
 
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def single_thread_sample(a, b, seconds: float = 4.0) -> dict:
+    """The reference's own dispatch: one caller thread (CpuDispatch
+    CallerThread / SingleThread, cpu.rs:1372-1374) running gemm_avx2 over a
+    row sample of the same GEMM."""
+    from oracle import oracle as O
+    n, k = b.shape[1], a.shape[1]
+    t0 = time.perf_counter()
+    O.gemm_avx2_restated(a[:1], b, 0, 1, 1)
+    per_row = max(time.perf_counter() - t0, 1e-4)
+    rows = max(1, min(a.shape[0], int(seconds / per_row)))
+    t0 = time.perf_counter()
+    O.gemm_avx2_restated(a[:rows], b, 0, rows, 1)
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * rows * n * k / dt / 1e12, "unit": "TFLOP/s", "cores": 1,
+            "sample": f"{rows} of {a.shape[0]} output rows, one thread (restated gemm_avx2), {dt:.1f} s"}
+
+
 def cpu_baseline_sample(a, b, bias, seconds: float):
     """The reference's CPU GEMM (gemm_avx2 loop structure, restated in oracle/)
-    on all host threads over a bounded row sample of the same workload."""
+    on all host threads over a bounded row sample of the same workload, plus
+    the single-thread figure of the reference's own dispatch."""
     from oracle import oracle as O
     O.build()
     n = a.shape[1]
@@ -147,7 +177,8 @@ def cpu_baseline_sample(a, b, bias, seconds: float):
     flops = 2.0 * rows_total * n * a.shape[1]
     return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
             "sample": f"{rows_total} of {a.shape[0]} output rows of the {a.shape[0]}x{n}x{a.shape[1]} GEMM "
-                      f"(restated gemm_avx2, -O3 -mavx2 -ffp-contract=off, row-sharded), {dt:.1f} s"}
+                      f"(restated gemm_avx2, -O3 -mavx2 -ffp-contract=off, row-sharded), {dt:.1f} s",
+            "cpu_model": cpu_model(), "single_thread": single_thread_sample(a, b)}
 
 
 def dist_init(args):
@@ -194,6 +225,7 @@ def run_reference(args, rank, world):
         step(rows)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
+    single_thread = single_thread_sample(a, b)
     flops = 2.0 * rows * n * n
     value = flops / t / 1e12
     line = {
@@ -204,7 +236,8 @@ def run_reference(args, rank, world):
         "config": workload_config(n, world),
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": nthreads, "kind": "port",
                          "sample": f"{rows} of {n} output rows per step (restated gemm_avx2 + bias + ReLU, "
-                                   f"row-sharded over {nthreads} threads)"},
+                                   f"row-sharded over {nthreads} threads)",
+                         "cpu_model": cpu_model(), "single_thread": single_thread},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -332,6 +365,31 @@ def run_workload(args, rank, world, local):
     if rank == 0:
         for line in lines:
             print(json.dumps(line), flush=True)
+
+
+def replica_digest(t):
+    """Order-independent digest of an f32 device tensor's bits: the wrapping
+    int64 sums of the words and of the words weighted by position."""
+    import torch
+    u = t.reshape(-1).view(torch.int32).to(torch.int64)
+    w = torch.arange(u.numel(), device=t.device, dtype=torch.int64) % 65521 + 1
+    return torch.stack([u.sum(), (u * w).sum()])
+
+
+def sampled_parity(out_t, a_h, b_h, bias_h, mode, nrows=32):
+    """Relative Frobenius error of `nrows` output rows (spread over the whole
+    matrix, first and last included) against the oracle."""
+    from oracle import oracle as O
+    O.build()
+    m = a_h.shape[0]
+    rows = np.unique(np.linspace(0, m - 1, nrows).astype(np.int64))
+    ref = O.matmul(a_h, b_h, bias=bias_h, epilogue=O.EPI_BIAS_RELU, rows=rows, nthreads=os.cpu_count() or 1)
+    got = out_t[rows.tolist()].cpu().numpy().astype(np.float64)
+    den = float(np.linalg.norm(ref.astype(np.float64)))
+    err = float(np.linalg.norm(got - ref) / (den if den > 0 else 1.0))
+    tol = 1e-5 if mode == "strict" else 2e-3
+    return {"rows": int(len(rows)), "rel_frob": err, "tol": tol, "ok": err <= tol,
+            "against": "oracle (restated reference gemm + bias + ReLU)"}
 
 
 def hg_panels(m, panels):
@@ -499,6 +557,20 @@ def main():
         hg.close()
     clocks.stop()
 
+    # ------------------------------------------------------ correctness
+    # After the timed regions (which leave the same result in place): every
+    # rank's replica must be identical, and rank 0 checks sampled output rows
+    # against the oracle (the restated reference CPU GEMM + bias + ReLU).
+    digest = replica_digest(out_t)
+    replicas_equal = None
+    if world > 1:
+        everyone = [torch.empty_like(digest) for _ in range(world)]
+        dist.all_gather(everyone, digest)
+        replicas_equal = all(bool(torch.equal(d, everyone[0])) for d in everyone)
+    parity = None
+    if rank == 0:
+        parity = sampled_parity(out_t, a_h, b_h, bias_h, args.mode)
+
     # ----------------------------------------------------------- roofline
     peaks = load_peaks()
     tf32_peak = peaks["bf16_tflops"] / 2.0
@@ -532,6 +604,8 @@ def main():
         "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms, "path": e2e_path},
         "clocks": clocks.summary(),
+        "parity": parity,
+        "replicas_equal": replicas_equal,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(a_h, b_h, bias_h, args.cpu_seconds)
