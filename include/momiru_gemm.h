@@ -59,7 +59,9 @@ enum {
                                      mapped from another rank's process      */
   MMR_ERR_TIMEOUT = 10,           /* bounded wait expired (host or device)   */
   MMR_ERR_DEVICE_FAULT_FLAG = 11, /* a kernel reported an error word         */
-  MMR_ERR_UNSUPPORTED_FAMILY = 12 /* forced kernel family cannot run this    */
+  MMR_ERR_UNSUPPORTED_FAMILY = 12, /* forced kernel family cannot run this   */
+  MMR_ERR_PLAN_MISMATCH = 13       /* a frozen launch record breaks a rule or
+                                      differs from what this library binds     */
 };
 
 /* ---- numeric mode (KernelMathMode, ir.rs:559-569; gated by the output's
@@ -98,15 +100,18 @@ enum {
   MMR_FAMILY_SIMT = 3     /* CUDA-core kernel, any strides; bit-exact order  */
 };
 
-#define MMR_MAX_RANK 4
+#define MMR_MAX_RANK 8 /* the reference tensor ranks: MIN_RANK 0 .. MAX_RANK 8 (tensor.rs:148-149) */
 
 /* A strided f32 view of a device buffer (Shape{dims,strides} + base offset).
- * Strides are in elements and may be 0 only on broadcast (extent-1) axes. */
+ * Strides are in elements and signed (a negative stride walks an axis
+ * backwards, as the reference's signed views do); the tensor-core and GEMV
+ * families need non-negative ones, the SIMT family takes any. */
 typedef struct mmr_view {
   uint64_t address;           /* device address of the bound buffer          */
   uint64_t bytes;             /* bytes of the bound buffer from `address`     */
   uint64_t base_offset_bytes; /* byte offset of element [0,..,0]              */
-  int32_t rank;               /* 1..MMR_MAX_RANK (0 = absent, for bias)       */
+  int32_t rank;               /* 1..MMR_MAX_RANK; 0 = a scalar output (vector
+                                 x vector), or an absent bias                 */
   int32_t device_ordinal;
   int64_t dims[MMR_MAX_RANK];
   int64_t strides[MMR_MAX_RANK];
@@ -142,6 +147,65 @@ typedef struct mmr_gemm_info {
 } mmr_gemm_info;
 
 typedef struct mmr_gemm_handle mmr_gemm_handle;
+
+/* ---- the frozen launch record ----------------------------------------------
+ * The fields of the reference's frozen GpuKernelPlan (plan.rs:941-1026) that
+ * this library decides for a node: launch shape, tiling, pipeline, TMEM and
+ * partition. Enum values follow the reference's enums: matrix_acceleration
+ * is MatrixAcceleration (0 None, 5 Tcgen05; plan.rs:757-772), async_copy is
+ * AsyncCopyKind (0 None, 4 Tma; plan.rs:629-639), partition is
+ * GpuPartitionKind (0 Grid, 1 SplitK, 2 StreamK, 3 PersistentCta;
+ * plan.rs:776-783). A plan that freezes a GPU MatMul node carries this record;
+ * mmr_gemm_bind_frozen binds the node only if the record obeys the GPU
+ * validator's rules (validation.rs:5630-5700, 5846-5911) and equals what the
+ * library launches, so no kernel, tile or schedule is substituted at bind. */
+enum { MMR_ACCEL_NONE = 0, MMR_ACCEL_TCGEN05 = 5 };
+enum { MMR_ASYNC_COPY_NONE = 0, MMR_ASYNC_COPY_TMA = 4 };
+enum { MMR_PARTITION_GRID = 0, MMR_PARTITION_SPLIT_K = 1, MMR_PARTITION_STREAM_K = 2,
+       MMR_PARTITION_PERSISTENT_CTA = 3 };
+
+typedef struct mmr_launch_record {
+  int32_t family;                  /* MMR_FAMILY_* the node binds              */
+  int32_t math_mode;               /* MMR_MATH_*                               */
+  int32_t grid[3], block[3], cluster[3];
+  int32_t dynamic_shared_bytes;
+  int32_t tmem_columns_per_cta;    /* 0: no tensor memory                      */
+  int32_t tmem_accumulator_stages;
+  int32_t tile_m, tile_n, tile_k;
+  int32_t pipeline_stages;
+  int32_t warps_per_block, producer_warps, consumer_warps;
+  int32_t matrix_acceleration;     /* MMR_ACCEL_*                              */
+  int32_t async_copy;              /* MMR_ASYNC_COPY_*                         */
+  int32_t tensor_maps;             /* TMA descriptors encoded at bind          */
+  int32_t partition;               /* MMR_PARTITION_*                          */
+  int32_t split_k;                 /* K parts per output tile (1 = unsplit)    */
+  int32_t stream_k_slices;         /* output tiles split stream-K style        */
+  int32_t persistent_ctas_per_sm;  /* 0: not persistent                        */
+  int32_t cluster_launch;          /* 1: launched as thread-block clusters     */
+  int32_t use_distributed_shared_memory;
+} mmr_launch_record;
+
+/* Host-only, touches no GPU: the record mmr_gemm_bind would freeze for `desc`
+ * on a device with `sm_count` SMs (148 on B200). */
+MMR_API int32_t mmr_gemm_plan_launch(const mmr_matmul_desc *desc, int32_t sm_count, mmr_launch_record *out);
+
+/* The record a bound handle launches with. */
+MMR_API int32_t mmr_gemm_launch_record(const mmr_gemm_handle *h, mmr_launch_record *out);
+
+/* Host-only: the GPU validator's rules on a frozen record alone -- tcgen05
+ * needs tensor memory; TMEM columns a power of two, a multiple of the
+ * 32-column allocation unit and at most 512; accumulator stages with TMEM;
+ * TMA needs tensor maps; clusters within 8 CTAs and launched as clusters;
+ * shared memory within 227 KB; block and warp counts consistent.
+ * MMR_ERR_PLAN_MISMATCH names the rule broken. */
+MMR_API int32_t mmr_check_launch_record(const mmr_launch_record *rec);
+
+/* Bind as mmr_gemm_bind does, but only to the launch `frozen` describes: the
+ * record must pass mmr_check_launch_record and equal, field by field, what
+ * this library binds for the node on this device; otherwise nothing is bound
+ * and MMR_ERR_PLAN_MISMATCH names the first differing field. */
+MMR_API int32_t mmr_gemm_bind_frozen(const mmr_matmul_desc *desc, const mmr_launch_record *frozen,
+                                     mmr_gemm_handle **out);
 
 /* Host-only validation of the MatMul contract and layout admission; touches no
  * GPU. Fills `info` (may be NULL). validation.rs:2300-2398, cpu.rs:613-714,

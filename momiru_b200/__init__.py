@@ -5,13 +5,13 @@ the C ABI in include/momiru_gemm.h; this package is the host-side mirror of
 the reference's node / bind / replay / quiesce interface.
 """
 from .execution import (AccuracyContract, BoundGemm, Epilogue, GpuGemmBackend, HostGemm, KernelFamily,
-                        KernelMathMode, MatMulNode, PlanError, matmul, output_dims, selftest_bounded_wait,
-                        shard_columns, validate)
+                        KernelMathMode, MatMulNode, PlanError, check_launch_record, matmul, output_dims,
+                        plan_launch, selftest_bounded_wait, shard_columns, validate)
 from .tensor import DeviceBuffer, DeviceView
 
 __all__ = [
     "AccuracyContract", "BoundGemm", "DeviceBuffer", "DeviceView", "Epilogue", "GpuGemmBackend", "HostGemm",
     "KernelFamily",
-    "KernelMathMode", "MatMulNode", "PlanError", "matmul", "output_dims", "selftest_bounded_wait", "shard_columns",
-    "validate",
+    "KernelMathMode", "MatMulNode", "PlanError", "check_launch_record", "matmul", "output_dims", "plan_launch",
+    "selftest_bounded_wait", "shard_columns", "validate",
 ]

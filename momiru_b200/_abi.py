@@ -9,7 +9,7 @@ from __future__ import annotations
 import ctypes
 import os
 
-MAX_RANK = 4
+MAX_RANK = 8
 
 # status codes
 OK = 0
@@ -25,6 +25,7 @@ ERR_PEER_ACCESS = 9
 ERR_TIMEOUT = 10
 ERR_DEVICE_FAULT_FLAG = 11
 ERR_UNSUPPORTED_FAMILY = 12
+ERR_PLAN_MISMATCH = 13
 
 MATH_STRICT_FP32, MATH_TF32, MATH_EXACT = 0, 1, 2
 EPI_NONE, EPI_BIAS, EPI_BIAS_RELU, EPI_RELU = 0, 1, 2, 3
@@ -38,8 +39,12 @@ EXPORTED = [
     "mmr_gemm_destroy", "mmr_gemm_query", "mmr_last_error", "mmr_version",
     "mmr_selftest_bounded_wait", "mmr_shard_columns", "mmr_gemm_run_noalloc",
     "mmr_ipc_export", "mmr_ipc_import", "mmr_ipc_release", "mmr_sharded_gemm_bind", "mmr_gemm_bind_host",
-    "mmr_shard_local_desc",
+    "mmr_shard_local_desc", "mmr_gemm_plan_launch", "mmr_gemm_launch_record", "mmr_check_launch_record",
+    "mmr_gemm_bind_frozen",
 ]
+ACCEL_NONE, ACCEL_TCGEN05 = 0, 5
+ASYNC_COPY_NONE, ASYNC_COPY_TMA = 0, 4
+PARTITION_GRID, PARTITION_SPLIT_K, PARTITION_STREAM_K, PARTITION_PERSISTENT_CTA = 0, 1, 2, 3
 NOALLOC_SCRATCH_BYTES = 64 * 1024
 NOALLOC_MAX_TILES = 8189
 
@@ -100,6 +105,43 @@ class MmrGemmInfo(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class MmrLaunchRecord(ctypes.Structure):
+    """mmr_launch_record: the GpuKernelPlan fields the library freezes."""
+    _fields_ = [
+        ("family", ctypes.c_int32),
+        ("math_mode", ctypes.c_int32),
+        ("grid", ctypes.c_int32 * 3),
+        ("block", ctypes.c_int32 * 3),
+        ("cluster", ctypes.c_int32 * 3),
+        ("dynamic_shared_bytes", ctypes.c_int32),
+        ("tmem_columns_per_cta", ctypes.c_int32),
+        ("tmem_accumulator_stages", ctypes.c_int32),
+        ("tile_m", ctypes.c_int32),
+        ("tile_n", ctypes.c_int32),
+        ("tile_k", ctypes.c_int32),
+        ("pipeline_stages", ctypes.c_int32),
+        ("warps_per_block", ctypes.c_int32),
+        ("producer_warps", ctypes.c_int32),
+        ("consumer_warps", ctypes.c_int32),
+        ("matrix_acceleration", ctypes.c_int32),
+        ("async_copy", ctypes.c_int32),
+        ("tensor_maps", ctypes.c_int32),
+        ("partition", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("stream_k_slices", ctypes.c_int32),
+        ("persistent_ctas_per_sm", ctypes.c_int32),
+        ("cluster_launch", ctypes.c_int32),
+        ("use_distributed_shared_memory", ctypes.c_int32),
+    ]
+
+    def as_dict(self) -> dict:
+        out = {}
+        for name, typ in self._fields_:
+            v = getattr(self, name)
+            out[name] = tuple(v) if hasattr(typ, "_length_") else v
+        return out
+
+
 class MmrIpcHandle(ctypes.Structure):
     _fields_ = [("bytes", ctypes.c_uint8 * 64), ("offset", ctypes.c_uint64)]
 
@@ -147,6 +189,10 @@ def load() -> ctypes.CDLL:
     lib.mmr_ipc_release.argtypes = [ctypes.c_uint64, P(MmrIpcHandle)]
     lib.mmr_sharded_gemm_bind.argtypes = [P(MmrShardedDesc), P(h)]
     lib.mmr_gemm_bind_host.argtypes = [P(MmrMatmulDesc), ctypes.c_int32, P(h)]
+    lib.mmr_gemm_plan_launch.argtypes = [P(MmrMatmulDesc), ctypes.c_int32, P(MmrLaunchRecord)]
+    lib.mmr_gemm_launch_record.argtypes = [h, P(MmrLaunchRecord)]
+    lib.mmr_check_launch_record.argtypes = [P(MmrLaunchRecord)]
+    lib.mmr_gemm_bind_frozen.argtypes = [P(MmrMatmulDesc), P(MmrLaunchRecord), P(h)]
     lib.mmr_shard_local_desc.argtypes = [P(MmrMatmulDesc), ctypes.c_int32, ctypes.c_int32, P(MmrMatmulDesc),
                                          P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_uint64)]
     lib.mmr_shard_columns.argtypes = [ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,

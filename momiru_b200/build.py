@@ -1,4 +1,8 @@
-"""Builds the in-tree CUDA library libmomiru_gemm.so for sm_100a with nvcc."""
+"""Builds the in-tree CUDA library libmomiru_gemm.so for sm_100a with nvcc.
+
+Each translation unit compiles to an object in parallel (the tcgen05 kernel
+families are split over four units), then nvcc links the shared library.
+"""
 from __future__ import annotations
 
 import os
@@ -9,8 +13,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libmomiru_gemm.so")
-SOURCES = ["momiru_gemm.cu"]
-HEADERS = ["ptx.cuh", "epilogue.cuh", "tc_gemm.cuh", "tc_gemm_2sm.cuh", "simt_gemm.cuh", "gemv.cuh"]
+SOURCES = ["momiru_gemm.cu", "tc_strict_pair.cu", "tc_tf32_pair.cu", "tc_strict_1cta.cu", "tc_tf32_1cta.cu"]
+HEADERS = ["ptx.cuh", "epilogue.cuh", "tc_gemm.cuh", "tc_gemm_2sm.cuh", "simt_gemm.cuh", "gemv.cuh", "fixup.cuh",
+           "tc_launch.h", "tc_launch.cuh"]
+OBJ_DIR = os.path.join(LIB_DIR, "obj")
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
@@ -38,12 +44,22 @@ def _stale() -> bool:
 def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> str:
     if not force and not _stale():
         return LIB_PATH
-    os.makedirs(LIB_DIR, exist_ok=True)
-    cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-shared", "-o", LIB_PATH,
-           *[os.path.join(CSRC, s) for s in SOURCES]]
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    jobs = []
+    for src in SOURCES:
+        obj = os.path.join(OBJ_DIR, os.path.splitext(src)[0] + ".o")
+        cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-c", "-o", obj, os.path.join(CSRC, src)]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        jobs.append((obj, subprocess.Popen(cmd)))
+    failed = [obj for obj, proc in jobs if proc.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, f"nvcc ({', '.join(os.path.basename(f) for f in failed)})")
+    link = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB_PATH,
+            *[obj for obj, _ in jobs]]
     if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
+        print(" ".join(link), file=sys.stderr)
+    subprocess.run(link, check=True)
     return LIB_PATH
 
 

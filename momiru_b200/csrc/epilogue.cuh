@@ -76,7 +76,7 @@ __device__ __forceinline__ double horner_one_rn(double x, const double (&c)[N]) 
 // [0, 1), [1, 8) and [8, 27] with their published coefficients (the same
 // constants as the reference, which the result depends on to the last bit),
 // 0 above 27, and exp(-x^2) from the math library.
-__device__ __noinline__ double erfc_nonnegative(double x) {
+static __device__ __noinline__ double erfc_nonnegative(double x) {
   constexpr double T[5] = {9.60497373987051638749e0, 9.00260197203842689217e1, 2.23200534594684319226e3,
                            7.00332514112805075473e3, 5.55923013010394962768e4};
   constexpr double U[5] = {3.35617141647503099647e1, 5.21357949780152679795e2, 4.59432382970980127987e3,
@@ -104,7 +104,7 @@ __device__ __noinline__ double erfc_nonnegative(double x) {
 
 // The activations other than ReLU: called out of line, once per element, from
 // epilogues that keep their accumulators in registers.
-__device__ __noinline__ float act_other(int act, float x) {
+static __device__ __noinline__ float act_other(int act, float x) {
   switch (act) {
     case ACT_RELU6:
       if (x != x) return x;

@@ -22,9 +22,10 @@
 #include "../../include/momiru_gemm.h"
 #include "gemv.cuh"
 #include "ptx.cuh"
+#include "fixup.cuh"
 #include "simt_gemm.cuh"
-#include "tc_gemm.cuh"
 #include "tc_gemm_2sm.cuh"
+#include "tc_launch.h"
 
 namespace {
 
@@ -60,17 +61,28 @@ struct DeviceGuard {
 
 // ------------------------------------------------------------- the plan --
 
-// A logical matrix operand: element (batch b0, b1, row r, col c) lives at
-// base + b0*s_b0 + b1*s_b1 + r*s_r + c*s_c (elements; s_* >= 0).
+// Batch axes a plan keeps after canonicalisation (a rank-8 view has six).
+constexpr int kMaxBatch = MMR_MAX_RANK - 2;
+static_assert(kMaxBatch == mmr::SIMT_MAX_BATCH, "the SIMT kernel indexes every batch axis a plan keeps");
+
+// A logical matrix operand: element (batch index i[0..nb), row r, col c)
+// lives at base + sum_j i[j]*s_b[j] + r*s_r + c*s_c (elements, signed;
+// s_b[j] = 0 where the operand is broadcast over batch axis j).
 struct Operand {
   uint64_t base = 0;  // device address of element [0,..,0]
-  int64_t s_b0 = 0, s_b1 = 0, s_r = 0, s_c = 0;
+  int64_t s_b[kMaxBatch] = {};
+  int64_t s_r = 0, s_c = 0;
   uint64_t lo = 0, hi = 0;  // byte range touched (for aliasing checks)
   uint64_t alloc = 0;
 };
 
 struct Plan {
-  int64_t batch0 = 1, batch1 = 1, m = 0, n = 0, k = 0;
+  // Batch axes of the output after canonicalisation: extent-1 axes dropped,
+  // neighbours merged wherever every operand walks them as one axis.
+  int nb = 0;
+  int64_t bdims[kMaxBatch] = {};
+  int64_t batch = 1;  // product of bdims
+  int64_t m = 0, n = 0, k = 0;
   Operand a, b, c;
   uint64_t bias = 0;
   int64_t bias_s = 0;
@@ -81,35 +93,46 @@ struct Plan {
   bool empty = false;  // nothing to compute (some output extent is zero)
 };
 
-int64_t extent_elems(const mmr_view& v) {
-  // Largest element offset + 1 (0 when any extent is 0).
-  int64_t span = 0;
+// Smallest and largest element offset a view reaches (strides may be
+// negative: a reversed axis); false when some extent is 0 (no element).
+bool view_span(const mmr_view& v, int64_t* lo, int64_t* hi) {
+  *lo = 0;
+  *hi = 0;
   for (int i = 0; i < v.rank; ++i) {
-    if (v.dims[i] == 0) return 0;
-    span += (v.dims[i] - 1) * v.strides[i];
+    if (v.dims[i] == 0) return false;
+    const int64_t reach = (v.dims[i] - 1) * v.strides[i];
+    if (reach < 0) *lo += reach; else *hi += reach;
   }
-  return span + 1;
+  return true;
 }
 
-int32_t check_view(const mmr_view& v, const char* name, int32_t device) {
-  if (v.rank < 1 || v.rank > MMR_MAX_RANK)
-    return fail(MMR_ERR_INVALID_SHAPE, "%s: rank %d outside 1..%d", name, v.rank, MMR_MAX_RANK);
+// Shape, alignment and bounds of one view (cpu.rs:613-714 restated for
+// device views). Rank 0 (a scalar) is admitted where `allow_scalar` is set:
+// the output of a vector-vector product (validation.rs:2355-2361).
+int32_t check_view(const mmr_view& v, const char* name, int32_t device, bool allow_scalar = false) {
+  const int min_rank = allow_scalar ? 0 : 1;
+  if (v.rank < min_rank || v.rank > MMR_MAX_RANK)
+    return fail(MMR_ERR_INVALID_SHAPE, "%s: rank %d outside %d..%d", name, v.rank, min_rank, MMR_MAX_RANK);
   for (int i = 0; i < v.rank; ++i) {
     if (v.dims[i] < 0) return fail(MMR_ERR_INVALID_SHAPE, "%s: negative extent on axis %d", name, i);
-    if (v.strides[i] < 0)
-      return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: negative stride on axis %d is not admitted", name, i);
     if (v.dims[i] > (int64_t(1) << 31) - 1)
       return fail(MMR_ERR_INVALID_SHAPE, "%s: extent %lld on axis %d exceeds 2^31-1", name,
                   (long long)v.dims[i], i);
+    if (v.strides[i] > (int64_t(1) << 40) || v.strides[i] < -(int64_t(1) << 40))
+      return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: stride on axis %d beyond 2^40 elements", name, i);
   }
   if (v.base_offset_bytes % 4 != 0)
     return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: base offset %llu is not f32-aligned", name,
                 (unsigned long long)v.base_offset_bytes);
   if (v.address % 4 != 0) return fail(MMR_ERR_UNSUPPORTED_LAYOUT, "%s: address is not f32-aligned", name);
-  const int64_t ext = extent_elems(v);
-  if (ext > 0) {
+  int64_t lo = 0, hi = 0;
+  if (view_span(v, &lo, &hi)) {
     if (v.address == 0) return fail(MMR_ERR_INVALID_ARGUMENT, "%s: null address", name);
-    const uint64_t need = v.base_offset_bytes + uint64_t(ext) * 4u;
+    const int64_t first = int64_t(v.base_offset_bytes / 4) + lo;
+    if (first < 0)
+      return fail(MMR_ERR_OUT_OF_BOUNDS, "%s: a negative stride reaches %lld elements before the buffer", name,
+                  (long long)-first);
+    const uint64_t need = v.base_offset_bytes + uint64_t(hi + 1) * 4u;
     if (need > v.bytes)
       return fail(MMR_ERR_OUT_OF_BOUNDS, "%s: view needs %llu bytes but the buffer has %llu", name,
                   (unsigned long long)need, (unsigned long long)v.bytes);
@@ -130,8 +153,14 @@ bool broadcast_extent(int64_t l, int64_t r, int64_t* out) {
 }
 
 void set_range(Operand& o, const mmr_view& v) {
-  o.lo = v.address + v.base_offset_bytes;
-  o.hi = o.lo + uint64_t(extent_elems(v)) * 4u;
+  int64_t lo = 0, hi = 0;
+  const uint64_t at = v.address + v.base_offset_bytes;
+  if (view_span(v, &lo, &hi)) {
+    o.lo = at + uint64_t(lo * 4);  // wraps correctly for lo < 0 (bounds checked)
+    o.hi = at + uint64_t((hi + 1) * 4);
+  } else {
+    o.lo = o.hi = at;
+  }
   o.alloc = v.allocation_id;
 }
 
@@ -160,7 +189,7 @@ int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
   int32_t rc;
   if ((rc = check_view(L, "lhs", d->device_ordinal))) return rc;
   if ((rc = check_view(R, "rhs", d->device_ordinal))) return rc;
-  if ((rc = check_view(O, "out", d->device_ordinal))) return rc;
+  if ((rc = check_view(O, "out", d->device_ordinal, true))) return rc;
 
   const int lr = L.rank, rr = R.rank;
   const bool ta = d->transpose_lhs != 0, tb = d->transpose_rhs != 0;
@@ -196,12 +225,16 @@ int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
   const int lbr = lv ? 0 : lr - 2, rbr = rv ? 0 : rr - 2;
   const int br = std::max(lbr, rbr);
   const int mat_rank = (lv ? 0 : 1) + (rv ? 0 : 1);
-  if (O.rank != br + mat_rank && !(br + mat_rank == 0 && O.rank == 1 && O.dims[0] == 1))
+  // The output's rank is exactly batch rank + matrix dims: a vector-vector
+  // product has a rank-0 (scalar) output (validation.rs:2355-2361).
+  if (O.rank != br + mat_rank)
     return fail(MMR_ERR_INVALID_SHAPE, "output rank %d, expected %d", O.rank, br + mat_rank);
-  if (br > 2) return fail(MMR_ERR_INVALID_SHAPE, "more than two batch axes");
 
-  int64_t bdims[2] = {1, 1};
-  int64_t as_b[2] = {0, 0}, bs_b[2] = {0, 0}, cs_b[2] = {0, 0};
+  // Batch axes, right-aligned (NumPy broadcast), each checked against the
+  // output; extent-1 axes index nothing and are dropped.
+  int nb = 0;
+  int64_t bdims[kMaxBatch];
+  int64_t as_b[kMaxBatch], bs_b[kMaxBatch], cs_b[kMaxBatch];
   for (int b = 0; b < br; ++b) {
     const int li = b - (br - lbr), ri = b - (br - rbr);
     const int64_t ld = li >= 0 ? L.dims[li] : 1, rd = ri >= 0 ? R.dims[ri] : 1;
@@ -212,12 +245,36 @@ int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
     if (O.dims[b] != e)
       return fail(MMR_ERR_INVALID_SHAPE, "output batch axis %d is %lld, expected %lld", b,
                   (long long)O.dims[b], (long long)e);
-    // Place batch axes right-aligned into the two slots (slot 1 = innermost).
-    const int slot = 2 - br + b;
-    bdims[slot] = e;
-    as_b[slot] = (li >= 0 && ld != 1) ? L.strides[li] : 0;
-    bs_b[slot] = (ri >= 0 && rd != 1) ? R.strides[ri] : 0;
-    cs_b[slot] = O.strides[b];
+    if (e == 1) continue;
+    bdims[nb] = e;
+    as_b[nb] = (li >= 0 && ld != 1) ? L.strides[li] : 0;
+    bs_b[nb] = (ri >= 0 && rd != 1) ? R.strides[ri] : 0;
+    cs_b[nb] = O.strides[b];
+    ++nb;
+  }
+  // Merge neighbouring axes that every operand walks as one (outer stride =
+  // inner stride x inner extent; broadcast axes have stride 0 on both).
+  for (int j = nb - 2; j >= 0; --j) {
+    const int64_t d1 = bdims[j + 1];
+    if (as_b[j] == as_b[j + 1] * d1 && bs_b[j] == bs_b[j + 1] * d1 && cs_b[j] == cs_b[j + 1] * d1) {
+      bdims[j] *= d1;
+      as_b[j] = as_b[j + 1];
+      bs_b[j] = bs_b[j + 1];
+      cs_b[j] = cs_b[j + 1];
+      for (int q = j + 1; q + 1 < nb; ++q) {
+        bdims[q] = bdims[q + 1];
+        as_b[q] = as_b[q + 1];
+        bs_b[q] = bs_b[q + 1];
+        cs_b[q] = cs_b[q + 1];
+      }
+      --nb;
+    }
+  }
+  int64_t batch = 1;
+  for (int j = 0; j < nb; ++j) {
+    if (bdims[j] > 0 && batch > (int64_t(1) << 40) / bdims[j])
+      return fail(MMR_ERR_INVALID_SHAPE, "batch of more than 2^40 matrices");
+    batch *= bdims[j];
   }
   int oax = br;
   if (!lv) {
@@ -233,9 +290,11 @@ int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
   }
   if (lv && !rv) C.s_r = 0;
   if (rv && !lv) { C.s_r = O.strides[br]; C.s_c = 0; }
-  A.s_b0 = as_b[0]; A.s_b1 = as_b[1];
-  B.s_b0 = bs_b[0]; B.s_b1 = bs_b[1];
-  C.s_b0 = cs_b[0]; C.s_b1 = cs_b[1];
+  for (int j = 0; j < nb; ++j) {
+    A.s_b[j] = as_b[j];
+    B.s_b[j] = bs_b[j];
+    C.s_b[j] = cs_b[j];
+  }
   set_range(A, L);
   set_range(B, R);
   set_range(C, O);
@@ -257,35 +316,34 @@ int32_t build_plan(const mmr_matmul_desc* d, Plan* p) {
     p->bias_s = V.strides[0];
   }
 
-  p->batch0 = bdims[0];
-  p->batch1 = bdims[1];
+  p->nb = nb;
+  for (int j = 0; j < nb; ++j) p->bdims[j] = bdims[j];
+  p->batch = batch;
   p->m = m;
   p->n = n;
   p->k = k1;
   p->a = A;
   p->b = B;
   p->c = C;
-  p->empty = (bdims[0] == 0 || bdims[1] == 0 || m == 0 || n == 0);
+  p->empty = (batch == 0 || m == 0 || n == 0);
   return MMR_OK;
 }
 
 // ---------------------------------------------------- family admission --
 
 // One batch axis for TMA: the operand is either broadcast over the whole
-// batch or indexed by the flattened batch index with a single stride.
+// batch or indexed by the flattened (row-major) batch index with a single
+// stride, i.e. its strides chain across every batch axis.
 bool flat_batch(const Plan& p, const Operand& o, int64_t* stride, bool* batched) {
-  const int64_t b0 = p.batch0, b1 = p.batch1;
-  const bool v0 = b0 > 1 && o.s_b0 != 0, v1 = b1 > 1 && o.s_b1 != 0;
-  if (!v0 && !v1) {
-    *batched = false;
-    *stride = 0;
-    return (b0 <= 1 || o.s_b0 == 0) && (b1 <= 1 || o.s_b1 == 0);
-  }
-  *batched = true;
-  if (b0 <= 1) { *stride = o.s_b1; return true; }
-  if (b1 <= 1) { *stride = o.s_b0; return true; }
-  if (v0 && v1 && o.s_b0 == o.s_b1 * b1) { *stride = o.s_b1; return true; }
-  return false;
+  bool any = false;
+  for (int j = 0; j < p.nb; ++j) any |= o.s_b[j] != 0;
+  *batched = any;
+  *stride = 0;
+  if (!any) return true;
+  for (int j = 0; j + 1 < p.nb; ++j)
+    if (o.s_b[j] != o.s_b[j + 1] * p.bdims[j + 1]) return false;
+  *stride = o.s_b[p.nb - 1];
+  return true;
 }
 
 struct TmaLayout {
@@ -307,8 +365,13 @@ TmaLayout tma_admission(const Plan& p) {
     t.why = "batch axes do not flatten to one strided axis";
     return t;
   }
-  const int64_t batch = p.batch0 * p.batch1;
+  const int64_t batch = p.batch;
   if (batch > 1 && !cb) { t.why = "output broadcast over the batch"; return t; }
+  if ((t.a_batched && t.a_sb <= 0) || (t.b_batched && t.b_sb <= 0) || (batch > 1 && t.c_sb <= 0)) {
+    t.why = "a negative batch stride (TMA walks forward only)";
+    return t;
+  }
+  if (p.bias && p.bias_s != 1) { t.why = "strided bias"; return t; }
   // A: K-contiguous (K-major) or M-contiguous (MN-major).
   if (p.a.s_c == 1 && (p.a.s_r % 4 == 0) && p.a.s_r > 0) t.a_mn = false;
   else if (p.a.s_r == 1 && (p.a.s_c % 4 == 0) && p.a.s_c > 0) t.a_mn = true;
@@ -331,7 +394,8 @@ TmaLayout tma_admission(const Plan& p) {
 }
 
 bool gemv_admission(const Plan& p, const char** why) {
-  if (p.batch0 * p.batch1 != 1) { *why = "batched"; return false; }
+  if (p.batch != 1) { *why = "batched"; return false; }
+  if (p.a.s_r < 0 || p.a.s_c < 0 || p.c.s_r < 0 || p.c.s_c < 0) { *why = "negative strides"; return false; }
   if (p.m < 1 || p.m > mmr::GV_MAX_M) { *why = "M outside 1..16"; return false; }
   if (p.k < 1 || p.k > int64_t(mmr::GV_KSPLIT) * mmr::GV_MAX_KSLICE) { *why = "K outside 1..8192"; return false; }
   if (p.n > INT32_MAX) { *why = "N too large"; return false; }
@@ -400,6 +464,33 @@ int32_t encode_3d(CUtensorMap* tm, uint64_t base, uint64_t inner, uint64_t outer
 
 }  // namespace
 
+namespace {
+
+// Every launch decision bind freezes for a node, derived on the host from the
+// plan and the device's SM count alone (no CUDA call): the fields of the
+// reference's frozen GpuKernelPlan (plan.rs:941-1026) that this library owns.
+struct Launch {
+  int32_t family = MMR_FAMILY_AUTO;
+  int mode = 0;         // tcgen05: 1 = 3xTF32, 0 = TF32
+  bool pair = false;    // tcgen05 on CTA pairs
+  uint32_t bk = 0;      // k-block width
+  int tile_m = 0, tile_n = 0, tile_k = 0;
+  int64_t tiles = 0;
+  int k_blocks = 0, chunk_kb = 0;
+  int64_t npairs = 0;   // CTA pairs launched (pair kernel)
+  int64_t split = 1;    // K parts per tile when there are fewer tiles than pairs
+  int sk_tiles = 0;     // trailing tiles split stream-K style
+  dim3 grid, block;
+  int smem = 0;
+  int cluster_x = 1, cluster_y = 1;
+  int stages = 0, warps = 0, producer_warps = 0, consumer_warps = 0;
+  int tmem_columns = 0, tmem_acc_stages = 0;
+  int gv_mt = 0, kslice = 0;
+  int tensor_maps = 0;
+};
+
+}  // namespace
+
 // ----------------------------------------------------------------- handle --
 
 struct mmr_gemm_handle {
@@ -428,6 +519,7 @@ struct mmr_gemm_handle {
   unsigned int* d_ws_count = nullptr;
   size_t ws_count_bytes = 0;
   int sms = 148;
+  Launch launch;  // the frozen launch decisions (mmr_gemm_launch_record)
   // column-sharded GEMM with replicated output
   bool sharded = false;
   int rank = 0, nranks = 1;
@@ -471,90 +563,6 @@ int32_t encode_tc_maps(mmr_gemm_handle* h, const Plan& p, const TmaLayout& t, in
   else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, bk, b_rows, "rhs");
   if (e) return e;
   return encode_3d(&h->tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out");
-}
-
-template <int MODE, bool AMN, bool BMN>
-cudaError_t launch_tc(mmr_gemm_handle* h, cudaStream_t s) {
-  mmr::tc_gemm_kernel<MODE, AMN, BMN><<<h->grid, h->block, h->smem, s>>>(h->tmA, h->tmB, h->tmC, h->tcp);
-  return cudaGetLastError();
-}
-
-// Sets the shared-memory opt-in and checks the register split: setmaxnreg.inc
-// waits until the block's launch registers (threads x compiled count) can
-// cover the request, so a split larger than that would never proceed. Such a
-// build is refused here instead of launched.
-template <int MODE, bool AMN, bool BMN>
-cudaError_t prepare_tc(int smem) {
-  using Cfg = mmr::TcConfig<MODE>;
-  cudaError_t e = cudaFuncSetAttribute(mmr::tc_gemm_kernel<MODE, AMN, BMN>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  cudaFuncAttributes fa;
-  e = cudaFuncGetAttributes(&fa, mmr::tc_gemm_kernel<MODE, AMN, BMN>);
-  if (e != cudaSuccess) return e;
-  const long need = 2L * 128 * Cfg::kEpiRegs + long(Cfg::kThreads - 256) * Cfg::kOtherRegs;
-  if (long(fa.numRegs) * Cfg::kThreads < need) return cudaErrorInvalidConfiguration;
-  return cudaSuccess;
-}
-
-template <int MODE, bool AMN, bool BMN>
-cudaError_t launch_tc2(mmr_gemm_handle* h, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = h->grid;
-  cfg.blockDim = h->block;
-  cfg.dynamicSmemBytes = h->smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mmr::tc_gemm_2sm_kernel<MODE, AMN, BMN>, h->tmA, h->tmB, h->tmC, h->tcp);
-}
-
-template <int MODE, bool AMN, bool BMN>
-cudaError_t prepare_tc2(int smem) {
-  using Cfg = mmr::Tc2Config<MODE>;
-  cudaError_t e = cudaFuncSetAttribute(mmr::tc_gemm_2sm_kernel<MODE, AMN, BMN>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return e;
-  cudaFuncAttributes fa;
-  e = cudaFuncGetAttributes(&fa, mmr::tc_gemm_2sm_kernel<MODE, AMN, BMN>);
-  if (e != cudaSuccess) return e;
-  const long need = 2L * 128 * Cfg::kEpiRegs + long(Cfg::kThreads - 256) * Cfg::kOtherRegs;
-  if (long(fa.numRegs) * Cfg::kThreads < need) return cudaErrorInvalidConfiguration;
-  return cudaSuccess;
-}
-
-using TcLaunch = cudaError_t (*)(mmr_gemm_handle*, cudaStream_t);
-using TcPrep = cudaError_t (*)(int);
-
-TcLaunch tc_launch_table(int mode, bool amn, bool bmn) {
-  static const TcLaunch t[2][2][2] = {
-      {{launch_tc<0, false, false>, launch_tc<0, false, true>}, {launch_tc<0, true, false>, launch_tc<0, true, true>}},
-      {{launch_tc<1, false, false>, launch_tc<1, false, true>}, {launch_tc<1, true, false>, launch_tc<1, true, true>}}};
-  return t[mode][amn][bmn];
-}
-TcLaunch tc2_launch_table(int mode, bool amn, bool bmn) {
-  static const TcLaunch t[2][2][2] = {
-      {{launch_tc2<0, false, false>, launch_tc2<0, false, true>}, {launch_tc2<0, true, false>, launch_tc2<0, true, true>}},
-      {{launch_tc2<1, false, false>, launch_tc2<1, false, true>}, {launch_tc2<1, true, false>, launch_tc2<1, true, true>}}};
-  return t[mode][amn][bmn];
-}
-TcPrep tc2_prep_table(int mode, bool amn, bool bmn) {
-  static const TcPrep t[2][2][2] = {
-      {{prepare_tc2<0, false, false>, prepare_tc2<0, false, true>}, {prepare_tc2<0, true, false>, prepare_tc2<0, true, true>}},
-      {{prepare_tc2<1, false, false>, prepare_tc2<1, false, true>}, {prepare_tc2<1, true, false>, prepare_tc2<1, true, true>}}};
-  return t[mode][amn][bmn];
-}
-
-TcPrep tc_prep_table(int mode, bool amn, bool bmn) {
-  static const TcPrep t[2][2][2] = {
-      {{prepare_tc<0, false, false>, prepare_tc<0, false, true>}, {prepare_tc<0, true, false>, prepare_tc<0, true, true>}},
-      {{prepare_tc<1, false, false>, prepare_tc<1, false, true>}, {prepare_tc<1, true, false>, prepare_tc<1, true, true>}}};
-  return t[mode][amn][bmn];
 }
 
 template <int MT>
@@ -605,14 +613,19 @@ void fill_simt_params(const Plan& p, mmr::SimtParams* sp) {
   s.m = int(p.m);
   s.n = int(p.n);
   s.k = int(p.k);
-  s.batch0 = int(p.batch0);
-  s.batch1 = int(p.batch1);
+  s.nb = p.nb;
+  for (int j = 0; j < mmr::SIMT_MAX_BATCH; ++j) {
+    s.bdims[j] = j < p.nb ? int(p.bdims[j]) : 1;
+    s.a_bs[j] = j < p.nb ? p.a.s_b[j] : 0;
+    s.b_bs[j] = j < p.nb ? p.b.s_b[j] : 0;
+    s.c_bs[j] = j < p.nb ? p.c.s_b[j] : 0;
+  }
   s.a = reinterpret_cast<const float*>(p.a.base);
-  s.a_b0 = p.a.s_b0; s.a_b1 = p.a.s_b1; s.a_m = p.a.s_r; s.a_k = p.a.s_c;
+  s.a_m = p.a.s_r; s.a_k = p.a.s_c;
   s.b = reinterpret_cast<const float*>(p.b.base);
-  s.b_b0 = p.b.s_b0; s.b_b1 = p.b.s_b1; s.b_k = p.b.s_r; s.b_n = p.b.s_c;
+  s.b_k = p.b.s_r; s.b_n = p.b.s_c;
   s.c = reinterpret_cast<float*>(p.c.base);
-  s.c_b0 = p.c.s_b0; s.c_b1 = p.c.s_b1; s.c_m = p.c.s_r; s.c_n = p.c.s_c;
+  s.c_m = p.c.s_r; s.c_n = p.c.s_c;
   s.bias = reinterpret_cast<const float*>(p.bias);
   s.bias_n = p.bias_s;
   s.epilogue = p.epilogue;
@@ -620,7 +633,7 @@ void fill_simt_params(const Plan& p, mmr::SimtParams* sp) {
 
 void fill_info_common(const Plan& p, mmr_gemm_info* info) {
   info->math_mode = p.math;
-  info->batch = p.batch0 * p.batch1;
+  info->batch = p.batch;
   info->m = p.m;
   info->n = p.n;
   info->k = p.k;
@@ -629,7 +642,7 @@ void fill_info_common(const Plan& p, mmr_gemm_info* info) {
 
 // Algorithmic HBM bytes: every operand element read once, C written once.
 double algorithmic_bytes(const Plan& p, bool a_batched, bool b_batched) {
-  const double batch = double(p.batch0 * p.batch1);
+  const double batch = double(p.batch);
   const double a = double(p.m) * double(p.k) * (a_batched ? batch : 1.0);
   const double b = double(p.k) * double(p.n) * (b_batched ? batch : 1.0);
   const double c = double(p.m) * double(p.n) * batch;
@@ -657,6 +670,180 @@ int32_t choose_family(const Plan& p, const TmaLayout& t, int32_t* family) {
     if (!gemv_ok) return fail(MMR_ERR_UNSUPPORTED_FAMILY, "GEMV family not admissible: %s", gemv_why);
   }
   *family = p.family;
+  return MMR_OK;
+}
+
+int32_t derive_launch(const Plan& p, const TmaLayout& t, int32_t fam, int sms, Launch* out) {
+  Launch L;
+  L.family = fam;
+  const int64_t batch = p.batch;
+  if (p.empty) {
+    *out = L;
+    return MMR_OK;
+  }
+  if (fam == MMR_FAMILY_TCGEN05) {
+    L.mode = (p.math == MMR_MATH_STRICT_FP32) ? 1 : 0;
+    // Both modes run on CTA pairs (256-row tiles) unless M fits one 128-row tile.
+    L.pair = p.m > mmr::TC_BM;
+    L.bk = L.pair ? (L.mode ? mmr::Tc2Config<1>::kBK : mmr::Tc2Config<0>::kBK)
+                  : (L.mode ? mmr::TcConfig<1>::kBK : mmr::TcConfig<0>::kBK);
+    L.tile_m = L.pair ? 2 * mmr::TC_BM : mmr::TC_BM;
+    L.tile_n = mmr::TC_BN;
+    L.tile_k = int(L.bk);
+    const int64_t tiles_m = (p.m + L.tile_m - 1) / L.tile_m, tiles_n = (p.n + mmr::TC_BN - 1) / mmr::TC_BN;
+    L.tiles = tiles_m * tiles_n * batch;
+    if (L.tiles > INT32_MAX) return fail(MMR_ERR_INVALID_SHAPE, "too many output tiles");
+    L.k_blocks = int((p.k + L.bk - 1) / L.bk);
+    // StrictFp32 sums K in chunks of 256 with round-to-nearest adds; one TF32
+    // pass keeps a single chain per tile.
+    L.chunk_kb = L.mode ? int(256 / L.bk) : L.k_blocks;
+    L.tensor_maps = 3;
+    L.tmem_columns = 512;
+    L.tmem_acc_stages = 2;
+    L.producer_warps = 1;
+    if (L.pair) {
+      L.smem = L.mode ? mmr::Tc2Config<1>::kSmemBytes : mmr::Tc2Config<0>::kSmemBytes;
+      // Fewer tiles than pairs and a long K: split each tile along K over
+      // several pairs, stream-K style, in parts of at least 128 k-blocks. A
+      // split tile costs on the order of 10 us per part over the unsplit
+      // one (measured: 1024^2 x 8192 in 4 parts 319 -> 145 us, but 512^3 in
+      // 4 parts of 8 k-blocks 35 -> 72 us), so short parts do not pay.
+      L.split = L.tiles < sms / 2
+                    ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / L.tiles, L.k_blocks / 128))
+                    : 1;
+      L.npairs = std::min<int64_t>(L.tiles, sms / 2) * L.split;
+      L.grid = dim3(unsigned(2 * L.npairs));
+      // Whole rounds of tiles stay round-robin. When the tiles do not fill
+      // the last round, that round is split stream-K; when it is less than
+      // half full, the round before it is split too, so that no tile is cut
+      // into more pieces than about three pairs.
+      const int64_t rem = L.tiles % L.npairs;
+      L.sk_tiles = L.npairs > L.tiles ? int(L.tiles) : rem == 0 ? 0 : int(2 * rem >= L.npairs ? rem : L.npairs + rem);
+      L.block = dim3(L.mode ? mmr::Tc2Config<1>::kThreads : mmr::Tc2Config<0>::kThreads);
+      L.cluster_x = 2;
+      L.stages = L.mode ? mmr::Tc2Config<1>::kStages : mmr::Tc2Config<0>::kStages;
+    } else {
+      L.smem = L.mode ? mmr::TcConfig<1>::kSmemBytes : mmr::TcConfig<0>::kSmemBytes;
+      L.grid = dim3(unsigned(std::min<int64_t>(L.tiles, sms)));
+      L.block = dim3(L.mode ? mmr::TcConfig<1>::kThreads : mmr::TcConfig<0>::kThreads);
+      L.stages = L.mode ? mmr::TcConfig<1>::kStages : mmr::TcConfig<0>::kStages;
+    }
+    L.warps = int(L.block.x / 32);
+    L.consumer_warps = L.warps - 2;  // epilogue (+ split) warps beside the producer and the MMA issuer
+  } else if (fam == MMR_FAMILY_GEMV) {
+    int kslice = int((p.k + mmr::GV_KSPLIT - 1) / mmr::GV_KSPLIT);
+    L.kslice = (kslice + mmr::GV_ROWS - 1) / mmr::GV_ROWS * mmr::GV_ROWS;
+    L.gv_mt = p.m <= 1 ? 1 : p.m <= 2 ? 2 : p.m <= 4 ? 4 : p.m <= 8 ? 8 : 16;
+    L.smem = mmr::gemv_smem_bytes(L.gv_mt, L.kslice);
+    L.grid = dim3(unsigned((p.n + mmr::GV_COLS - 1) / mmr::GV_COLS), mmr::GV_KSPLIT, 1);
+    L.block = dim3(mmr::GV_THREADS);
+    L.cluster_y = mmr::GV_KSPLIT;
+    L.stages = mmr::GV_STAGES;
+    L.warps = mmr::GV_THREADS / 32;
+    L.producer_warps = 1;
+    L.consumer_warps = L.warps - 1;
+    L.tile_m = L.gv_mt;
+    L.tile_n = mmr::GV_COLS;
+    L.tile_k = L.kslice;
+    L.tensor_maps = 1;
+  } else {
+    if (batch > 65535) return fail(MMR_ERR_INVALID_SHAPE, "batch too large for the SIMT family");
+    L.grid = dim3(unsigned((p.n + mmr::SIMT_BN - 1) / mmr::SIMT_BN), unsigned((p.m + mmr::SIMT_BM - 1) / mmr::SIMT_BM),
+                  unsigned(batch));
+    if (L.grid.y > 65535) return fail(MMR_ERR_INVALID_SHAPE, "M too large for the SIMT family");
+    L.block = dim3(256);
+    L.tile_m = mmr::SIMT_BM;
+    L.tile_n = mmr::SIMT_BN;
+    L.tile_k = mmr::SIMT_BK;
+    L.warps = 8;
+    L.consumer_warps = 8;
+    L.stages = 1;
+  }
+  *out = L;
+  return MMR_OK;
+}
+
+void to_record(const Launch& L, int32_t math, mmr_launch_record* r) {
+  memset(r, 0, sizeof *r);
+  r->family = L.family;
+  r->math_mode = math;
+  r->grid[0] = int32_t(L.grid.x);
+  r->grid[1] = int32_t(L.grid.y);
+  r->grid[2] = int32_t(L.grid.z);
+  r->block[0] = int32_t(L.block.x);
+  r->block[1] = int32_t(L.block.y);
+  r->block[2] = int32_t(L.block.z);
+  r->cluster[0] = L.cluster_x;
+  r->cluster[1] = L.cluster_y;
+  r->cluster[2] = 1;
+  r->dynamic_shared_bytes = L.smem;
+  r->tmem_columns_per_cta = L.tmem_columns;
+  r->tmem_accumulator_stages = L.tmem_acc_stages;
+  r->tile_m = L.tile_m;
+  r->tile_n = L.tile_n;
+  r->tile_k = L.tile_k;
+  r->pipeline_stages = L.stages;
+  r->warps_per_block = L.warps;
+  r->producer_warps = L.producer_warps;
+  r->consumer_warps = L.consumer_warps;
+  const bool tc = L.family == MMR_FAMILY_TCGEN05;
+  r->matrix_acceleration = tc ? MMR_ACCEL_TCGEN05 : MMR_ACCEL_NONE;
+  r->async_copy = L.tensor_maps > 0 ? MMR_ASYNC_COPY_TMA : MMR_ASYNC_COPY_NONE;
+  r->tensor_maps = L.tensor_maps;
+  if (tc) {
+    r->partition = L.sk_tiles > 0 ? MMR_PARTITION_STREAM_K : MMR_PARTITION_PERSISTENT_CTA;
+    r->split_k = int32_t(L.split);
+    r->stream_k_slices = L.sk_tiles;
+    r->persistent_ctas_per_sm = 1;
+  } else if (L.family == MMR_FAMILY_GEMV) {
+    r->partition = MMR_PARTITION_SPLIT_K;  // K over the CTAs of a cluster, reduced in DSMEM
+    r->split_k = mmr::GV_KSPLIT;
+    r->use_distributed_shared_memory = 1;
+  } else {
+    r->partition = MMR_PARTITION_GRID;
+    r->split_k = 1;
+  }
+  r->cluster_launch = (L.cluster_x * L.cluster_y > 1) ? 1 : 0;
+}
+
+// The GPU validator's rules on a frozen record (validation.rs:5630-5700,
+// 5846-5911, restated for the fields this record carries; B200 limits:
+// 512 TMEM columns per CTA in units of 32, 227 KB of shared memory per block,
+// portable clusters of at most 8 CTAs).
+int32_t check_record_rules(const mmr_launch_record& r) {
+  auto bad = [](const char* why) { return fail(MMR_ERR_PLAN_MISMATCH, "frozen launch record: %s", why); };
+  if (r.family < MMR_FAMILY_TCGEN05 || r.family > MMR_FAMILY_SIMT) return bad("family is not a bound kernel family");
+  if (r.math_mode < MMR_MATH_STRICT_FP32 || r.math_mode > MMR_MATH_EXACT) return bad("unknown math mode");
+  for (int i = 0; i < 3; ++i)
+    if (r.grid[i] < 0 || r.block[i] < 1 || r.cluster[i] < 1) return bad("grid, block and cluster extents");
+  const long threads = long(r.block[0]) * r.block[1] * r.block[2];
+  if (threads > 1024) return bad("more than 1024 threads per block");
+  if (r.warps_per_block != (threads + 31) / 32) return bad("warps_per_block differs from the block size");
+  if (r.producer_warps < 0 || r.consumer_warps < 0 || r.producer_warps + r.consumer_warps > r.warps_per_block)
+    return bad("producer and consumer warps exceed the block");
+  if (r.dynamic_shared_bytes < 0 || r.dynamic_shared_bytes > 232448) return bad("dynamic shared memory above 227 KB");
+  const int cl = r.cluster[0] * r.cluster[1] * r.cluster[2];
+  if (cl > 8) return bad("cluster of more than 8 CTAs (non-portable)");
+  if ((cl > 1) != (r.cluster_launch != 0)) return bad("cluster dims and cluster_launch disagree");
+  for (int i = 0; i < 3; ++i)
+    if (r.cluster[i] > 1 && r.grid[i] % r.cluster[i] != 0) return bad("grid is not a whole number of clusters");
+  const bool uses_tmem = r.tmem_columns_per_cta > 0 || r.tmem_accumulator_stages > 0;
+  if (uses_tmem) {
+    if (r.tmem_columns_per_cta <= 0 || r.tmem_accumulator_stages <= 0 || r.tmem_columns_per_cta > 512)
+      return bad("TMEM columns must be 1..512 with at least one accumulator stage");
+    if (r.tmem_columns_per_cta % 32 != 0 || (r.tmem_columns_per_cta & (r.tmem_columns_per_cta - 1)) != 0)
+      return bad("TMEM columns must be a power of two and a multiple of 32");
+  }
+  if (r.matrix_acceleration == MMR_ACCEL_TCGEN05 && !uses_tmem) return bad("tcgen05 without tensor memory");
+  if (r.matrix_acceleration != MMR_ACCEL_TCGEN05 && r.matrix_acceleration != MMR_ACCEL_NONE)
+    return bad("matrix acceleration other than none or tcgen05");
+  if (r.async_copy == MMR_ASYNC_COPY_TMA && r.tensor_maps < 1) return bad("TMA without tensor maps");
+  if (r.async_copy != MMR_ASYNC_COPY_TMA && r.tensor_maps != 0) return bad("tensor maps without TMA");
+  if (r.async_copy != MMR_ASYNC_COPY_TMA && r.async_copy != MMR_ASYNC_COPY_NONE)
+    return bad("async copy other than none or TMA");
+  if (r.partition < MMR_PARTITION_GRID || r.partition > MMR_PARTITION_PERSISTENT_CTA) return bad("unknown partition");
+  if (r.split_k < 1 || r.stream_k_slices < 0) return bad("split_k below 1 or negative stream-K slices");
+  if (r.tile_m < 1 || r.tile_n < 1 || r.tile_k < 1 || r.pipeline_stages < 1) return bad("tile or stage count below 1");
   return MMR_OK;
 }
 
@@ -723,7 +910,7 @@ int32_t noalloc_setup(int dev, NoAllocDevice** out) {
     const int smem = mmr::TcConfig<1>::kSmemBytes;
     for (int amn = 0; amn < 2; ++amn)
       for (int bmn = 0; bmn < 2; ++bmn) {
-        e = tc_prep_table(1, amn, bmn)(smem);
+        e = mmr::tc_prepare(1, false, amn, bmn, smem);
         if (e != cudaSuccess)
           return fail(MMR_ERR_CUDA, "preparing the 3xTF32 kernel: %s", cudaGetErrorString(e));
       }
@@ -824,18 +1011,20 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     return MMR_OK;
   }
 
-  const int64_t batch = p.batch0 * p.batch1;
+  const int64_t batch = p.batch;
+  Launch L;
+  if ((rc = derive_launch(p, t, fam, sms, &L))) return cleanup(rc);
+  h->launch = L;
+  h->grid = L.grid;
+  h->block = L.block;
+  h->smem = L.smem;
+  h->sms = sms;
   if (fam == MMR_FAMILY_TCGEN05) {
-    h->mode = (p.math == MMR_MATH_STRICT_FP32) ? 1 : 0;
-    // Both modes run on CTA pairs (256-row tiles) unless M fits one 128-row tile.
-    h->pair = p.m > mmr::TC_BM;
+    h->mode = L.mode;
+    h->pair = L.pair;
     h->a_mn = t.a_mn;
     h->b_mn = t.b_mn;
-    const uint32_t bk = h->mode ? mmr::TcConfig<1>::kBK : mmr::TcConfig<0>::kBK;
-    static_assert(mmr::TcConfig<1>::kBK == mmr::Tc2Config<1>::kBK && mmr::TcConfig<0>::kBK == mmr::Tc2Config<0>::kBK,
-                  "one k-block width per mode");
-    const int tile_m = h->pair ? 2 * mmr::TC_BM : mmr::TC_BM;
-    int32_t e = encode_tc_maps(h, p, t, batch, bk, h->pair ? 128u : uint32_t(mmr::TC_BN));
+    int32_t e = encode_tc_maps(h, p, t, batch, L.bk, L.pair ? 128u : uint32_t(mmr::TC_BN));
     if (e) return cleanup(e);
 
     mmr::TcParams& q = h->tcp;
@@ -843,16 +1032,12 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     q.n = int(p.n);
     q.k = int(p.k);
     q.batch = int(batch);
-    q.tile_m = tile_m;
-    q.tiles_m = int((p.m + tile_m - 1) / tile_m);
+    q.tile_m = L.tile_m;
+    q.tiles_m = int((p.m + L.tile_m - 1) / L.tile_m);
     q.tiles_n = int((p.n + mmr::TC_BN - 1) / mmr::TC_BN);
-    const int64_t tiles = int64_t(q.tiles_m) * q.tiles_n * batch;
-    if (tiles > INT32_MAX) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "too many output tiles"));
-    q.tiles_total = int(tiles);
-    q.k_blocks = int((p.k + bk - 1) / bk);
-    // StrictFp32 sums K in chunks of 256 with round-to-nearest adds; one TF32
-    // pass keeps a single chain per tile.
-    q.chunk_kb = h->mode ? int(256 / bk) : q.k_blocks;
+    q.tiles_total = int(L.tiles);
+    q.k_blocks = L.k_blocks;
+    q.chunk_kb = L.chunk_kb;
     q.c = reinterpret_cast<float*>(p.c.base);
     q.c_ld = p.c.s_r;
     q.c_bs = t.c_sb;
@@ -863,74 +1048,47 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     q.err = h->d_err;
     q.timeout_ns = h->wait_timeout_ns;
     q.nf = nullptr;
+    q.sk_tiles = L.sk_tiles;
     if (h->mode == 1) {
-      const size_t words = 2 + 2 * size_t(tiles);
+      const size_t words = 2 + 2 * size_t(L.tiles);
       if (cudaMalloc(&h->d_nf, words * sizeof(unsigned int)) != cudaSuccess ||
           cudaMemset(h->d_nf, 0, words * sizeof(unsigned int)) != cudaSuccess)
         return cleanup(fail(MMR_ERR_CUDA, "allocating the non-finite bookkeeping failed"));
       q.nf = h->d_nf;
       fill_simt_params(p, &h->sp);
     }
-    h->sms = sms;
-    cudaError_t ce;
     if (h->pair) {
-      h->smem = h->mode ? mmr::Tc2Config<1>::kSmemBytes : mmr::Tc2Config<0>::kSmemBytes;
-      // Fewer tiles than pairs and a long K: split each tile along K over
-      // several pairs, stream-K style, in parts of at least 128 k-blocks. A
-      // split tile costs on the order of 10 us per part over the unsplit
-      // one (measured: 1024^2 x 8192 in 4 parts 319 -> 145 us, but 512^3 in
-      // 4 parts of 8 k-blocks 35 -> 72 us), so short parts do not pay.
-      const int64_t split =
-          tiles < sms / 2 ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / tiles, q.k_blocks / 128)) : 1;
-      const int64_t npairs = std::min<int64_t>(tiles, sms / 2) * split;
-      h->grid = dim3(unsigned(2 * npairs));
       // Stream-K workspace: two partial-sum slots per pair, and an arrival
       // counter per split tile (fewer than two rounds of them) and epilogue
       // warp of each CTA.
-      const size_t ws_bytes = size_t(npairs) * 2 * mmr::kSkSlotFloats * sizeof(float);
-      h->ws_count_bytes = size_t(2 * npairs) * 2 * mmr::TC_EPI_WARPS * sizeof(unsigned int);
+      const size_t ws_bytes = size_t(L.npairs) * 2 * mmr::kSkSlotFloats * sizeof(float);
+      h->ws_count_bytes = size_t(2 * L.npairs) * 2 * mmr::TC_EPI_WARPS * sizeof(unsigned int);
       if (cudaMalloc(&h->d_ws, ws_bytes) != cudaSuccess ||
           cudaMalloc(&h->d_ws_count, h->ws_count_bytes) != cudaSuccess ||
           cudaMemset(h->d_ws_count, 0, h->ws_count_bytes) != cudaSuccess)
         return cleanup(fail(MMR_ERR_CUDA, "allocating the stream-K workspace failed"));
       q.ws = h->d_ws;
       q.ws_count = h->d_ws_count;
-      // Whole rounds of tiles stay round-robin. When the tiles do not fill
-      // the last round, that round is split stream-K; when it is less than
-      // half full, the round before it is split too, so that no tile is cut
-      // into more pieces than about three pairs.
-      const int64_t rem = tiles % npairs;
-      q.sk_tiles = npairs > tiles ? int(tiles) : rem == 0 ? 0 : int(2 * rem >= npairs ? rem : npairs + rem);
-      h->block = dim3(h->mode ? mmr::Tc2Config<1>::kThreads : mmr::Tc2Config<0>::kThreads);
-      ce = tc2_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
-      h->info.cluster = 2;
-      h->info.stages = mmr::Tc2Config<1>::kStages;
-    } else {
-      h->smem = h->mode ? mmr::TcConfig<1>::kSmemBytes : mmr::TcConfig<0>::kSmemBytes;
-      h->grid = dim3(unsigned(std::min<int64_t>(tiles, sms)));
-      h->block = dim3(h->mode ? mmr::TcConfig<1>::kThreads : mmr::TcConfig<0>::kThreads);
-      ce = tc_prep_table(h->mode, t.a_mn, t.b_mn)(h->smem);
-      h->info.cluster = 1;
-      h->info.stages = h->mode ? mmr::TcConfig<1>::kStages : mmr::TcConfig<0>::kStages;
     }
+    const cudaError_t ce = mmr::tc_prepare(h->mode, h->pair, t.a_mn, t.b_mn, h->smem);
     if (ce == cudaErrorInvalidConfiguration)
       return cleanup(fail(MMR_ERR_CUDA, "tcgen05 kernel was compiled with too few registers for its warp split"));
     if (ce != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(ce)));
+    h->info.cluster = L.cluster_x;
+    h->info.stages = L.stages;
     h->info.a_mn_major = t.a_mn;
     h->info.b_mn_major = t.b_mn;
-    h->info.tile_m = tile_m;
-    h->info.tile_n = mmr::TC_BN;
-    h->info.tile_k = int(bk);
-    h->info.tiles = tiles;
+    h->info.tile_m = L.tile_m;
+    h->info.tile_n = L.tile_n;
+    h->info.tile_k = L.tile_k;
+    h->info.tiles = L.tiles;
     h->info.bytes = algorithmic_bytes(p, t.a_batched, t.b_batched);
   } else if (fam == MMR_FAMILY_GEMV) {
     mmr::GemvParams& g = h->gvp;
     g.m = int(p.m);
     g.n = int(p.n);
     g.k = int(p.k);
-    int kslice = int((p.k + mmr::GV_KSPLIT - 1) / mmr::GV_KSPLIT);
-    kslice = (kslice + mmr::GV_ROWS - 1) / mmr::GV_ROWS * mmr::GV_ROWS;
-    g.kslice = kslice;
+    g.kslice = L.kslice;
     g.a = reinterpret_cast<const float*>(p.a.base);
     g.a_m = p.a.s_r;
     g.a_k = p.a.s_c;
@@ -943,25 +1101,13 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     if (int32_t e = encode_3d(&h->tmB, p.b.base, p.n, p.k, 1, p.b.s_r, 0, mmr::GV_COLS, mmr::GV_ROWS, "rhs",
                               false, true))
       return cleanup(e);
-    h->gv_mt = p.m <= 1 ? 1 : p.m <= 2 ? 2 : p.m <= 4 ? 4 : p.m <= 8 ? 8 : 16;
-    h->smem = mmr::gemv_smem_bytes(h->gv_mt, kslice);
-    h->grid = dim3(unsigned((p.n + mmr::GV_COLS - 1) / mmr::GV_COLS), mmr::GV_KSPLIT, 1);
-    h->block = dim3(mmr::GV_THREADS);
+    h->gv_mt = L.gv_mt;
     cudaError_t ce = prepare_gemv(h->gv_mt, h->smem);
     if (ce != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaFuncSetAttribute(gemv): %s", cudaGetErrorString(ce)));
     h->info.bytes = algorithmic_bytes(p, true, true);
     h->info.cluster = mmr::GV_KSPLIT;
-  }
-  if (fam == MMR_FAMILY_SIMT) {
-    h->family = fam;
-    h->info.family = fam;
+  } else {
     fill_simt_params(p, &h->sp);
-    if (batch > 65535) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "batch too large for the SIMT family"));
-    h->grid = dim3(unsigned((p.n + mmr::SIMT_BN - 1) / mmr::SIMT_BN), unsigned((p.m + mmr::SIMT_BM - 1) / mmr::SIMT_BM),
-                   unsigned(batch));
-    if (h->grid.y > 65535) return cleanup(fail(MMR_ERR_INVALID_SHAPE, "M too large for the SIMT family"));
-    h->block = dim3(256);
-    h->smem = 0;
     h->info.bytes = algorithmic_bytes(p, true, true);
   }
   h->info.grid = int(h->grid.x * h->grid.y * h->grid.z);
@@ -1064,7 +1210,8 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
   if (!h->plan.empty) {
     switch (h->family) {
       case MMR_FAMILY_TCGEN05:
-        e = h->pair ? tc2_launch_table(h->mode, h->a_mn, h->b_mn)(h, s) : tc_launch_table(h->mode, h->a_mn, h->b_mn)(h, s);
+        e = mmr::tc_launch(h->mode, h->pair, h->a_mn, h->b_mn, mmr::TcShape{h->grid, h->block, h->smem}, s, h->tmA,
+                           h->tmB, h->tmC, h->tcp);
         if (e == cudaSuccess && h->mode == 1) {
           mmr::tc_nonfinite_fixup_kernel<<<h->sms, 256, 0, s>>>(h->sp, h->tcp);
           e = cudaGetLastError();
@@ -1241,7 +1388,7 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
     return MMR_OK;
   }
   if (!t.ok) return fail(MMR_ERR_UNSUPPORTED_FAMILY, "tcgen05 family not admissible: %s", t.why);
-  const int64_t batch = p.batch0 * p.batch1;
+  const int64_t batch = p.batch;
   const int64_t tiles_m = (p.m + mmr::TC_BM - 1) / mmr::TC_BM;
   const int64_t tiles_n = (p.n + mmr::TC_BN - 1) / mmr::TC_BN;
   const int64_t tiles = tiles_m * tiles_n * batch;
@@ -1317,7 +1464,8 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   // Clear what the kernels expect at zero: the error word, the flagged-tile
   // count and done counter, and this problem's per-tile flags.
   MMR_CUDA_TRY(cudaMemsetAsync(dev->scratch, 0, (6 + size_t(tiles)) * sizeof(unsigned int), s));
-  cudaError_t ce = tc_launch_table(1, t.a_mn, t.b_mn)(&h, s);
+  cudaError_t ce = mmr::tc_launch(1, false, t.a_mn, t.b_mn, mmr::TcShape{h.grid, h.block, h.smem}, s, h.tmA, h.tmB,
+                                  h.tmC, h.tcp);
   if (ce == cudaSuccess) {
     mmr::tc_nonfinite_fixup_kernel<<<dev->sms, 256, 0, s>>>(h.sp, h.tcp);
     ce = cudaGetLastError();
@@ -1466,7 +1614,10 @@ int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc* d, mmr_gemm_handle** out) 
   // epilogue behind the links together. (With more tiles than that, the
   // round-robin order keeps its L2 reuse.) The counters cover the split: the
   // bind sized them for up to two rounds.
-  if (h->pair && q > 0 && h->tcp.tiles_total < int(h->grid.x)) h->tcp.sk_tiles = h->tcp.tiles_total;
+  if (h->pair && q > 0 && h->tcp.tiles_total < int(h->grid.x)) {
+    h->tcp.sk_tiles = h->tcp.tiles_total;
+    h->launch.sk_tiles = h->tcp.sk_tiles;
+  }
   *out = h;
   return MMR_OK;
 }
@@ -1583,6 +1734,86 @@ int32_t mmr_gemm_bind_host(const mmr_matmul_desc* d, int32_t panels, mmr_gemm_ha
   h->ev_gemm.assign(size_t(np), nullptr);
   for (int64_t i = 0; ok && i < np; ++i) ok = make_event(&h->ev_lhs[i]) && make_event(&h->ev_gemm[i]);
   if (!ok) return cleanup(fail(MMR_ERR_CUDA, "cudaEventCreate failed"));
+  *out = h;
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_plan_launch(const mmr_matmul_desc* desc, int32_t sm_count, mmr_launch_record* out) {
+  if (!out) return fail(MMR_ERR_INVALID_ARGUMENT, "null launch record");
+  if (sm_count < 2 || sm_count > 1024) return fail(MMR_ERR_INVALID_ARGUMENT, "SM count %d outside 2..1024", sm_count);
+  Plan p;
+  int32_t rc = build_plan(desc, &p);
+  if (rc) return rc;
+  const TmaLayout t = tma_admission(p);
+  int32_t fam = MMR_FAMILY_AUTO;
+  if ((rc = choose_family(p, t, &fam))) return rc;
+  Launch L;
+  if ((rc = derive_launch(p, t, fam, sm_count, &L))) return rc;
+  to_record(L, p.math, out);
+  return MMR_OK;
+}
+
+int32_t mmr_gemm_launch_record(const mmr_gemm_handle* h, mmr_launch_record* out) {
+  if (!h || !out) return fail(MMR_ERR_INVALID_ARGUMENT, "null handle or launch record");
+  if (h->host) return fail(MMR_ERR_INVALID_ARGUMENT, "a host-buffer handle runs one bound GEMM per row panel");
+  to_record(h->launch, h->plan.math, out);
+  return MMR_OK;
+}
+
+int32_t mmr_check_launch_record(const mmr_launch_record* rec) {
+  if (!rec) return fail(MMR_ERR_INVALID_ARGUMENT, "null launch record");
+  return check_record_rules(*rec);
+}
+
+int32_t mmr_gemm_bind_frozen(const mmr_matmul_desc* desc, const mmr_launch_record* frozen, mmr_gemm_handle** out) {
+  if (!out || !frozen) return fail(MMR_ERR_INVALID_ARGUMENT, "null launch record or output handle");
+  *out = nullptr;
+  int32_t rc = check_record_rules(*frozen);
+  if (rc) return rc;
+  mmr_gemm_handle* h = nullptr;
+  if ((rc = mmr_gemm_bind(desc, &h))) return rc;
+  mmr_launch_record mine;
+  to_record(h->launch, h->plan.math, &mine);
+  struct Field {
+    const char* name;
+    const int32_t *a, *b;
+    int n;
+  };
+  const Field fields[] = {
+      {"family", &frozen->family, &mine.family, 1},
+      {"math_mode", &frozen->math_mode, &mine.math_mode, 1},
+      {"grid", frozen->grid, mine.grid, 3},
+      {"block", frozen->block, mine.block, 3},
+      {"cluster", frozen->cluster, mine.cluster, 3},
+      {"dynamic_shared_bytes", &frozen->dynamic_shared_bytes, &mine.dynamic_shared_bytes, 1},
+      {"tmem_columns_per_cta", &frozen->tmem_columns_per_cta, &mine.tmem_columns_per_cta, 1},
+      {"tmem_accumulator_stages", &frozen->tmem_accumulator_stages, &mine.tmem_accumulator_stages, 1},
+      {"tile_m", &frozen->tile_m, &mine.tile_m, 1},
+      {"tile_n", &frozen->tile_n, &mine.tile_n, 1},
+      {"tile_k", &frozen->tile_k, &mine.tile_k, 1},
+      {"pipeline_stages", &frozen->pipeline_stages, &mine.pipeline_stages, 1},
+      {"warps_per_block", &frozen->warps_per_block, &mine.warps_per_block, 1},
+      {"producer_warps", &frozen->producer_warps, &mine.producer_warps, 1},
+      {"consumer_warps", &frozen->consumer_warps, &mine.consumer_warps, 1},
+      {"matrix_acceleration", &frozen->matrix_acceleration, &mine.matrix_acceleration, 1},
+      {"async_copy", &frozen->async_copy, &mine.async_copy, 1},
+      {"tensor_maps", &frozen->tensor_maps, &mine.tensor_maps, 1},
+      {"partition", &frozen->partition, &mine.partition, 1},
+      {"split_k", &frozen->split_k, &mine.split_k, 1},
+      {"stream_k_slices", &frozen->stream_k_slices, &mine.stream_k_slices, 1},
+      {"persistent_ctas_per_sm", &frozen->persistent_ctas_per_sm, &mine.persistent_ctas_per_sm, 1},
+      {"cluster_launch", &frozen->cluster_launch, &mine.cluster_launch, 1},
+      {"use_distributed_shared_memory", &frozen->use_distributed_shared_memory,
+       &mine.use_distributed_shared_memory, 1},
+  };
+  static_assert(sizeof(mmr_launch_record) == 30 * sizeof(int32_t), "every record field is compared");
+  for (const Field& f : fields)
+    for (int i = 0; i < f.n; ++i)
+      if (f.a[i] != f.b[i]) {
+        mmr_gemm_destroy(h);
+        return fail(MMR_ERR_PLAN_MISMATCH, "frozen launch record field %s[%d] is %d; this library binds %d", f.name, i,
+                    f.a[i], f.b[i]);
+      }
   *out = h;
   return MMR_OK;
 }

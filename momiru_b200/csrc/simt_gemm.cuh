@@ -5,9 +5,9 @@
 // p increasing -- the per-element order of gemm_dot_f32 / gemm_axpy_f32 /
 // gemm_avx2 (src/momiru/tensor_light/execution/cpu.rs:2989-3098). Results are
 // therefore bit-identical to the reference except for NaN payloads. Handles any
-// non-negative element strides, up to two batch axes with broadcast (stride 0),
-// K = 0 (+0 then the epilogue), and every shape. It serves MMR_MATH_EXACT and
-// the layouts TMA cannot describe.
+// element strides (negative ones too: reversed views), up to six batch axes
+// with broadcast (stride 0), K = 0 (+0 then the epilogue), and every shape. It
+// serves MMR_MATH_EXACT and the layouts TMA cannot describe.
 #pragma once
 #include <stdint.h>
 
@@ -15,12 +15,17 @@
 
 namespace mmr {
 
+constexpr int SIMT_MAX_BATCH = 6;
+
 struct SimtParams {
   int m, n, k;
-  int batch0, batch1;
-  const float* a; long long a_b0, a_b1, a_m, a_k;
-  const float* b; long long b_b0, b_b1, b_k, b_n;
-  float* c; long long c_b0, c_b1, c_m, c_n;
+  // Batch axes (outermost first); the flat batch index enumerates them in
+  // row-major order. Strides are in elements, 0 on broadcast axes.
+  int nb;
+  int bdims[SIMT_MAX_BATCH];
+  const float* a; long long a_bs[SIMT_MAX_BATCH], a_m, a_k;
+  const float* b; long long b_bs[SIMT_MAX_BATCH], b_k, b_n;
+  float* c; long long c_bs[SIMT_MAX_BATCH], c_m, c_n;
   const float* bias; long long bias_n;
   int epilogue;  // EPI_* (epilogue.cuh)
   // Replicas of C on other ranks (same element offsets), for the exact
@@ -36,10 +41,17 @@ constexpr int SIMT_BM = 64, SIMT_BN = 64, SIMT_BK = 16;
 __device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, int n0, int bz,
                                                  float (*As)[SIMT_BM + 4], float (*Bs)[SIMT_BN + 4]) {
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  const int b0 = bz / p.batch1, b1 = bz - (bz / p.batch1) * p.batch1;
-  const float* A = p.a + b0 * p.a_b0 + b1 * p.a_b1;
-  const float* B = p.b + b0 * p.b_b0 + b1 * p.b_b1;
-  float* C = p.c + b0 * p.c_b0 + b1 * p.c_b1;
+  long long ao = 0, bo = 0, co = 0;
+  for (int j = p.nb - 1, rem = bz; j >= 0; --j) {
+    const int i = rem % p.bdims[j];
+    rem /= p.bdims[j];
+    ao += i * p.a_bs[j];
+    bo += i * p.b_bs[j];
+    co += i * p.c_bs[j];
+  }
+  const float* A = p.a + ao;
+  const float* B = p.b + bo;
+  float* C = p.c + co;
 
   float acc[4][4];
 #pragma unroll
@@ -52,12 +64,12 @@ __device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, in
     for (int idx = threadIdx.x; idx < SIMT_BK * SIMT_BM; idx += 256) {
       const int kk = idx / SIMT_BM, mm = idx - kk * SIMT_BM;
       const int gm = m0 + mm, gk = k0 + kk;
-      As[kk][mm] = (gm < p.m && kk < kmax) ? A[gm * p.a_m + gk * p.a_k] : 0.0f;
+      As[kk][mm] = (gm < p.m && kk < kmax) ? A[(long long)gm * p.a_m + (long long)gk * p.a_k] : 0.0f;
     }
     for (int idx = threadIdx.x; idx < SIMT_BK * SIMT_BN; idx += 256) {
       const int kk = idx / SIMT_BN, nn = idx - kk * SIMT_BN;
       const int gn = n0 + nn, gk = k0 + kk;
-      Bs[kk][nn] = (gn < p.n && kk < kmax) ? B[gk * p.b_k + gn * p.b_n] : 0.0f;
+      Bs[kk][nn] = (gn < p.n && kk < kmax) ? B[(long long)gk * p.b_k + (long long)gn * p.b_n] : 0.0f;
     }
     __syncthreads();
     for (int kk = 0; kk < kmax; ++kk) {
@@ -85,11 +97,11 @@ __device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, in
       const int gn = n0 + tx * 4 + j;
       if (gn >= p.n) continue;
       float x = acc[i][j];
-      if (add_bias) x = __fadd_rn(x, p.bias[gn * p.bias_n]);
+      if (add_bias) x = __fadd_rn(x, p.bias[(long long)gn * p.bias_n]);
       x = act_apply(act, x);
-      C[gm * p.c_m + gn * p.c_n] = x;
+      C[(long long)gm * p.c_m + (long long)gn * p.c_n] = x;
       for (int q = 0; q < p.npeers; ++q)
-        p.peer_c[q][b0 * p.c_b0 + b1 * p.c_b1 + gm * p.c_m + gn * p.c_n] = x;
+        p.peer_c[q][co + gm * p.c_m + gn * p.c_n] = x;
     }
   }
 }

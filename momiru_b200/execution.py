@@ -98,11 +98,12 @@ class PeerAccessError(PlanError): code = _abi.ERR_PEER_ACCESS
 class QuiescenceTimeout(PlanError): code = _abi.ERR_TIMEOUT
 class DeviceErrorFlag(PlanError): code = _abi.ERR_DEVICE_FAULT_FLAG
 class UnsupportedFamily(PlanError): code = _abi.ERR_UNSUPPORTED_FAMILY
+class PlanMismatch(PlanError): code = _abi.ERR_PLAN_MISMATCH
 
 
 _BY_CODE = {c.code: c for c in (InvalidArgument, InvalidShape, UnsupportedLayout, UnsafeAliasing,
                                 InvalidAccuracyContract, UnsupportedDevice, OutOfBounds, CudaError, PeerAccessError,
-                                QuiescenceTimeout, DeviceErrorFlag, UnsupportedFamily)}
+                                QuiescenceTimeout, DeviceErrorFlag, UnsupportedFamily, PlanMismatch)}
 
 
 def _check(rc: int) -> None:
@@ -169,18 +170,41 @@ def validate(node: MatMulNode, lhs: DeviceView, rhs: DeviceView, out: DeviceView
     return info.as_dict()
 
 
+def plan_launch(node: MatMulNode, lhs: DeviceView, rhs: DeviceView, out: DeviceView,
+                bias: DeviceView | None = None, sm_count: int = 148) -> _abi.MmrLaunchRecord:
+    """The launch record bind would freeze for this node on a device with
+    `sm_count` SMs (host only): what a plan's GpuKernelPlan carries for it."""
+    rec = _abi.MmrLaunchRecord()
+    _check(_abi.load().mmr_gemm_plan_launch(ctypes.byref(_desc(node, lhs, rhs, out, bias, None)), sm_count,
+                                            ctypes.byref(rec)))
+    return rec
+
+
+def check_launch_record(rec: _abi.MmrLaunchRecord) -> None:
+    """The GPU validator's rules on a frozen launch record (host only)."""
+    _check(_abi.load().mmr_check_launch_record(ctypes.byref(rec)))
+
+
 class BoundGemm:
-    """A bound GPU MatMul node (BoundBackend for one frozen node)."""
+    """A bound GPU MatMul node (BoundBackend for one frozen node).
+
+    With `frozen` (an MmrLaunchRecord from the plan), the node binds only to
+    exactly that launch; any difference raises PlanMismatch."""
 
     def __init__(self, node: MatMulNode, lhs: DeviceView, rhs: DeviceView, out: DeviceView,
-                 bias: DeviceView | None = None, stream: int | None = None):
+                 bias: DeviceView | None = None, stream: int | None = None,
+                 frozen: _abi.MmrLaunchRecord | None = None):
         self._lib = _abi.load()
         self.node = node
         # Keep the views (and so their buffers) alive for the handle's lifetime.
         self._views = (lhs, rhs, out, bias)
         self._handle = ctypes.c_void_p()
         desc = _desc(node, lhs, rhs, out, bias, stream)
-        _check(self._lib.mmr_gemm_bind(ctypes.byref(desc), ctypes.byref(self._handle)))
+        if frozen is None:
+            _check(self._lib.mmr_gemm_bind(ctypes.byref(desc), ctypes.byref(self._handle)))
+        else:
+            _check(self._lib.mmr_gemm_bind_frozen(ctypes.byref(desc), ctypes.byref(frozen),
+                                                  ctypes.byref(self._handle)))
         info = _abi.MmrGemmInfo()
         _check(self._lib.mmr_gemm_query(self._handle, ctypes.byref(info)))
         self.info = info.as_dict()
@@ -188,6 +212,11 @@ class BoundGemm:
     @property
     def family(self) -> str:
         return _abi.FAMILY_NAMES[self.info["family"]]
+
+    def launch_record(self) -> _abi.MmrLaunchRecord:
+        rec = _abi.MmrLaunchRecord()
+        _check(self._lib.mmr_gemm_launch_record(self._handle, ctypes.byref(rec)))
+        return rec
 
     def replay(self, stream: int | None = None) -> None:
         if not self._handle:
@@ -365,7 +394,7 @@ def matmul(lhs: DeviceView, rhs: DeviceView, bias: DeviceView | None = None, nod
     node = node or MatMulNode()
     if out is None:
         dims = output_dims(node, lhs, rhs)
-        out = DeviceView.empty(dims if dims else (1,), lhs.buffer.device_ordinal)
+        out = DeviceView.empty(dims, lhs.buffer.device_ordinal)
     with BoundGemm(node, lhs, rhs, out, bias, stream) as g:
         g.replay()
         g.quiesce_or_abort(timeout_s)

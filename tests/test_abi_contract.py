@@ -84,7 +84,11 @@ def test_unaligned_layouts_fall_back_to_simt_or_reject_forced_family():
     ((3, 4), (4, 5), (3, 5), True),
     ((4,), (4, 5), (5,), True),              # rank-1 lhs: promoted dim removed
     ((3, 4), (4,), (3,), True),              # rank-1 rhs
-    ((4,), (4,), (1,), True),                # dot -> scalar (held as [1])
+    ((4,), (4,), (), True),                  # dot -> rank-0 scalar (validation.rs:2355-2361)
+    ((4,), (4,), (1,), False),               # ... and not a rank-1 [1]
+    ((2, 1, 3, 2, 5, 4), (3, 1, 4, 6), (2, 1, 3, 2, 5, 6), True),      # rank 6 x rank 4
+    ((2, 1, 2, 1, 2, 1, 3, 4), (2, 1, 2, 1, 2, 4, 5), (2, 2, 2, 2, 2, 2, 3, 5), True),  # rank 8 x rank 7
+    ((2, 1, 2, 1, 2, 1, 3, 4), (3, 1, 2, 1, 2, 1, 4, 5), (3, 1, 2, 1, 2, 1, 3, 5), False),  # 2 vs 3
     ((2, 3, 4), (4, 5), (2, 3, 5), True),    # broadcast rhs
     ((1, 3, 4), (6, 4, 5), (6, 3, 5), True),  # 1 vs 6 -> 6
     ((0, 3, 4), (1, 4, 5), (0, 3, 5), True),  # 0 vs 1 -> 0 (not max)
@@ -132,15 +136,27 @@ def test_aliasing_bounds_alignment_device():
     other = DeviceView.contiguous(DeviceBuffer(6 * G, 4 * 64 * 64, 1), (64, 64))
     with pytest.raises(execution.UnsupportedDevice):
         validate(MatMulNode(), a, other, fake((64, 64), 3))
-    # negative strides are not admitted
+    # negative strides (a reversed view) are admitted on the SIMT family only
     neg = DeviceView(DeviceBuffer(7 * G, 4 * 64 * 64, 0), (64, 64), (64, -1), 63)
-    with pytest.raises(execution.UnsupportedLayout):
-        validate(MatMulNode(), a, neg, fake((64, 64), 3))
+    assert validate(MatMulNode(), a, neg, fake((64, 64), 3))["family"] == _abi.FAMILY_SIMT
+    with pytest.raises(execution.UnsupportedFamily):
+        validate(MatMulNode(family=KernelFamily.Tcgen05), a, neg, fake((64, 64), 3))
+    # ... and must stay inside the buffer: element [0, 63] would be 1 before it
+    before = DeviceView(DeviceBuffer(7 * G, 4 * 64 * 64, 0), (64, 64), (64, -1), 62)
+    with pytest.raises(execution.OutOfBounds):
+        validate(MatMulNode(), a, before, fake((64, 64), 3))
 
 
 def test_bias_contract():
     n = MatMulNode(epilogue=Epilogue.BIAS)
     validate(n, fake((8, 4), 1), fake((4, 16), 2), fake((8, 16), 3), fake((16,), 4))
+    # a strided bias view: not the tensor-core family (its epilogue reads the
+    # bias contiguously), the SIMT family takes it
+    sb = DeviceView(DeviceBuffer(8 * G, 4 * 32, 0), (16,), (2,), 0)
+    views = (fake((300, 64), 1), fake((64, 16), 2), fake((300, 16), 3))
+    assert validate(n, *views, sb)["family"] == _abi.FAMILY_SIMT
+    with pytest.raises(execution.UnsupportedFamily):
+        validate(MatMulNode(epilogue=Epilogue.BIAS, family=KernelFamily.Tcgen05), *views, sb)
     with pytest.raises(execution.InvalidShape):
         validate(n, fake((8, 4), 1), fake((4, 16), 2), fake((8, 16), 3), fake((8,), 4))
 
@@ -253,13 +269,14 @@ def _numpy_matmul_dims(lhs, rhs, tl, tr):
 
 
 def test_shape_contract_matches_numpy_matmul_on_random_shapes():
-    """Random ranks 1-4, extents 0-3 (0 and 1 included, so both broadcast
+    """Random ranks 1-8, extents 0-3 (0 and 1 included, so both broadcast
     rules and empty batches occur), transpose flags: the validator accepts
-    exactly the shapes NumPy matmul accepts and only with NumPy's output dims."""
+    exactly the shapes NumPy matmul accepts and only with NumPy's output dims
+    (a vector-vector product included, whose output is rank 0)."""
     from hypothesis import given, settings, strategies as st
-    dims = st.lists(st.integers(0, 3), min_size=1, max_size=4)
+    dims = st.lists(st.integers(0, 3), min_size=1, max_size=8)
 
-    @settings(max_examples=300, deadline=None, derandomize=True)
+    @settings(max_examples=600, deadline=None, derandomize=True)
     @given(dims, dims, st.booleans(), st.booleans(), st.integers(0, 2))
     def check(lhs, rhs, tl, tr, bump):
         want = _numpy_matmul_dims(tuple(lhs), tuple(rhs), tl, tr)
@@ -269,14 +286,72 @@ def test_shape_contract_matches_numpy_matmul_on_random_shapes():
             with pytest.raises(PlanError):
                 validate(node, fake(lhs, 1), fake(rhs, 2), fake(out or (1,), 3))
             return
-        if len(want) == 0 or len(want) > 4:
-            return  # scalar results and rank > 4 are outside the view ABI
         validate(node, fake(lhs, 1), fake(rhs, 2), fake(want, 3))
         assert execution.output_dims(node, fake(lhs, 1), fake(rhs, 2)) == tuple(want)
-        if bump:  # any other output extent is refused
+        if bump and want:  # any other output extent is refused
             wrong = list(want)
             wrong[bump % len(wrong)] += 1
             with pytest.raises(PlanError):
                 validate(node, fake(lhs, 1), fake(rhs, 2), fake(tuple(wrong), 3))
 
     check()
+
+
+# ------------------------------------------------ frozen launch records --
+def test_plan_launch_records_the_bound_launch_for_each_family():
+    """The record bind would freeze, derived on the host for a 148-SM device:
+    the 8192^3 node on CTA pairs (cluster 2, 256x256 tiles, 512 TMEM
+    columns, TMA), the skinny-M node on the GEMV family (8-CTA clusters,
+    split K), an exact node on the SIMT family (a grid, no TMA, no TMEM)."""
+    from momiru_b200 import check_launch_record, plan_launch
+    r = plan_launch(MatMulNode(epilogue=Epilogue.BIAS_RELU), fake((8192, 8192), 1), fake((8192, 8192), 2),
+                    fake((8192, 8192), 3), fake((8192,), 4))
+    assert r.family == _abi.FAMILY_TCGEN05 and r.matrix_acceleration == _abi.ACCEL_TCGEN05
+    assert tuple(r.cluster) == (2, 1, 1) and r.cluster_launch == 1 and r.grid[0] == 148
+    assert (r.tile_m, r.tile_n) == (256, 256) and r.tmem_columns_per_cta == 512 and r.tmem_accumulator_stages == 2
+    assert r.async_copy == _abi.ASYNC_COPY_TMA and r.tensor_maps == 3 and r.producer_warps == 1
+    assert r.partition == _abi.PARTITION_STREAM_K and r.stream_k_slices > 0 and r.persistent_ctas_per_sm == 1
+    check_launch_record(r)
+    g = plan_launch(MatMulNode(), fake((16, 4096), 1), fake((4096, 4096), 2), fake((16, 4096), 3))
+    assert g.family == _abi.FAMILY_GEMV and tuple(g.cluster) == (1, 8, 1) and g.partition == _abi.PARTITION_SPLIT_K
+    assert g.use_distributed_shared_memory == 1 and g.tmem_columns_per_cta == 0
+    check_launch_record(g)
+    e = plan_launch(MatMulNode(math_mode=KernelMathMode.Exact, accuracy=AccuracyContract.Exact), fake((100, 64), 1),
+                    fake((64, 200), 2), fake((100, 200), 3))
+    assert e.family == _abi.FAMILY_SIMT and e.async_copy == _abi.ASYNC_COPY_NONE and tuple(e.grid) == (4, 2, 1)
+    check_launch_record(e)
+    # small output with a long K: tiles split along K over several pairs
+    s = plan_launch(MatMulNode(), fake((1024, 8192), 1), fake((8192, 1024), 2), fake((1024, 1024), 3))
+    assert s.split_k > 1 and s.grid[0] == 2 * 16 * s.split_k
+
+
+def test_check_launch_record_enforces_the_gpu_validator_rules():
+    """validation.rs:5846-5911 on the record: tcgen05 needs TMEM, TMEM columns
+    a power of two and a multiple of 32 up to 512, TMA needs tensor maps,
+    clusters up to 8 and launched as clusters, shared memory within 227 KB."""
+    from momiru_b200 import check_launch_record, plan_launch
+    from momiru_b200.execution import PlanMismatch
+    base = plan_launch(MatMulNode(), fake((4096, 4096), 1), fake((4096, 4096), 2), fake((4096, 4096), 3))
+    check_launch_record(base)
+
+    def broken(**kw):
+        r = _abi.MmrLaunchRecord.from_buffer_copy(base)
+        for k, v in kw.items():
+            if isinstance(v, tuple):
+                getattr(r, k)[:] = v
+            else:
+                setattr(r, k, v)
+        with pytest.raises(PlanMismatch):
+            check_launch_record(r)
+
+    broken(tmem_columns_per_cta=0, tmem_accumulator_stages=0)   # tcgen05 without TMEM
+    broken(tmem_columns_per_cta=384)                            # not a power of two
+    broken(tmem_columns_per_cta=1024)                           # above 512
+    broken(tmem_columns_per_cta=16)                             # below the 32-column unit
+    broken(tensor_maps=0)                                       # TMA without maps
+    broken(cluster=(16, 1, 1))                                  # non-portable cluster
+    broken(cluster_launch=0)                                    # cluster dims without a cluster launch
+    broken(dynamic_shared_bytes=240 * 1024)                     # above 227 KB
+    broken(warps_per_block=3)                                   # inconsistent with the block
+    broken(matrix_acceleration=4)                               # wgmma is not an sm_100a path
+    broken(split_k=0)

@@ -573,3 +573,117 @@ def test_tf32_operands_are_truncated_by_the_tensor_core(oracle):
     raw, _ = run(TF32, DeviceView.from_host(a), DeviceView.from_host(b))
     trunc, _ = run(TF32, DeviceView.from_host(at), DeviceView.from_host(bt))
     assert np.array_equal(raw.view(np.uint32), trunc.view(np.uint32))
+
+
+# ------------------------------------------- ranks 0 and 5-8, signed views --
+def _batched_oracle(oracle, a, b, bias=None, epilogue=0):
+    """The oracle over NumPy-broadcast batch axes, one 2-D product per entry."""
+    shape = np.broadcast_shapes(a.shape[:-2], b.shape[:-2])
+    out = np.empty(shape + (a.shape[-2], b.shape[-1]), np.float32)
+    ab = np.broadcast_to(a, shape + a.shape[-2:])
+    bb = np.broadcast_to(b, shape + b.shape[-2:])
+    for idx in np.ndindex(*shape):
+        out[idx] = oracle.matmul(np.ascontiguousarray(ab[idx]), np.ascontiguousarray(bb[idx]), bias=bias,
+                                 epilogue=epilogue)
+    return out
+
+
+def test_vector_dot_has_a_rank0_output_bit_exact(oracle):
+    """[K] . [K] -> a rank-0 output (validation.rs:2355-2361), in the
+    reference's exact order, in both the Exact and the default StrictFp32
+    node (which binds the exact CUDA-core family for this shape)."""
+    a = rng.randn((4096,), 51)
+    b = rng.randn((4096,), 52)
+    ref = oracle.matmul(a.reshape(1, -1), b.reshape(-1, 1))[0, 0]
+    for nd in (EXACT, STRICT):
+        out = DeviceView.empty(())
+        with BoundGemm(nd, DeviceView.from_host(a), DeviceView.from_host(b), out) as g:
+            assert g.family == "simt"
+            g.replay()
+            g.quiesce_or_abort(30)
+        got = out.to_host()
+        assert got.shape == ()
+        assert got.view(np.uint32) == np.float32(ref).view(np.uint32)
+
+
+@pytest.mark.parametrize("lhs,rhs,fam", [
+    ((2, 1, 3, 1, 2, 1, 16, 24), (1, 2, 1, 2, 1, 2, 24, 20), "simt"),  # rank 8, broadcast on alternate axes
+    ((2, 3, 4, 64, 32), (2, 3, 4, 32, 48), "tcgen05"),                  # rank 5: batch axes merge into one
+    ((1, 2, 1, 3, 40, 36), (36, 72), "tcgen05"),                        # rank 6 x rank 2: rhs broadcast
+])
+def test_batched_ranks_up_to_eight(oracle, lhs, rhs, fam):
+    a = rng.randn(lhs, 53, 0.5)
+    b = rng.randn(rhs, 54, 0.5)
+    ref = _batched_oracle(oracle, a, b)
+    got, f = run(STRICT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert f == fam
+    assert got.shape == ref.shape
+    assert rel_frob(got, ref) <= STRICT_TOL
+    got, f = run(EXACT, DeviceView.from_host(a), DeviceView.from_host(b))
+    assert f == "simt" and np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_negative_strides_run_on_the_exact_family(oracle):
+    """A reversed-rows lhs view and a reversed-columns rhs view (signed
+    strides, as the reference's signed views give): admitted on the SIMT
+    family, bit-identical to the oracle on the logical matrices; the
+    tensor-core family refuses them."""
+    m, k, n = 70, 48, 90
+    a = rng.randn((m, k), 55)
+    b = rng.randn((k, n), 56)
+    bias = rng.randn((n,), 57, 0.1)
+    ra = DeviceView.from_host(np.ascontiguousarray(a[::-1]))
+    rb = DeviceView.from_host(np.ascontiguousarray(b[:, ::-1]))
+    av = DeviceView(ra.buffer, (m, k), (-k, 1), (m - 1) * k)
+    bv = DeviceView(rb.buffer, (k, n), (n, -1), n - 1)
+    ref = oracle.matmul(a, b, bias=bias, epilogue=oracle.EPI_BIAS_RELU)
+    for nd in (EXACT, STRICT):
+        got, f = run(node(nd, epilogue=Epilogue.BIAS_RELU), av, bv, DeviceView.from_host(bias))
+        assert f == "simt"
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    with pytest.raises(execution.UnsupportedFamily):
+        run(node(STRICT, family=KernelFamily.Tcgen05), av, bv)
+
+
+def test_strided_bias_binds_the_exact_family(oracle):
+    """A bias read with stride 2: the tensor-core epilogue reads the bias
+    contiguously, so the node binds the SIMT family, which is exact."""
+    m, k, n = 300, 64, 200
+    a = rng.randn((m, k), 58)
+    b = rng.randn((k, n), 59)
+    bias2 = rng.randn((2 * n,), 60, 0.1)
+    bb = DeviceView.from_host(bias2)
+    bias_view = DeviceView(bb.buffer, (n,), (2,), 0)
+    ref = oracle.matmul(a, b, bias=np.ascontiguousarray(bias2[::2]), epilogue=oracle.EPI_BIAS)
+    got, f = run(node(STRICT, epilogue=Epilogue.BIAS), DeviceView.from_host(a), padded(b), bias_view)
+    assert f == "simt"
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_bind_frozen_takes_exactly_the_planned_launch(oracle):
+    """A plan's frozen launch record (here the host-derived one) binds and
+    runs; the same record with one field changed is refused at bind with
+    PlanMismatch and nothing is bound."""
+    import torch
+    from momiru_b200 import plan_launch
+    from momiru_b200.execution import PlanMismatch
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    a = rng.randu((600, 384), 61)
+    b = rng.randu((384, 520), 62)
+    bias = rng.randn((520,), 63, 0.1)
+    da, db, dbias = DeviceView.from_host(a), padded(b), DeviceView.from_host(bias)
+    out = padded(np.zeros((600, 520), np.float32))
+    nd = node(STRICT, epilogue=Epilogue.BIAS_RELU)
+    rec = plan_launch(nd, da, db, out, dbias, sm_count=sms)
+    with BoundGemm(nd, da, db, out, dbias, frozen=rec) as g:
+        assert g.launch_record().as_dict() == rec.as_dict()
+        g.replay()
+        g.quiesce_or_abort(30)
+    ref = oracle.matmul(a, b, bias=bias, epilogue=oracle.EPI_BIAS_RELU)
+    assert rel_frob(out.to_host(), ref) <= STRICT_TOL
+    for field, value in (("tile_k", rec.tile_k * 2), ("pipeline_stages", rec.pipeline_stages + 1),
+                         ("stream_k_slices", rec.stream_k_slices + 1)):
+        other = _abi.MmrLaunchRecord.from_buffer_copy(rec)
+        setattr(other, field, value)
+        with pytest.raises(PlanMismatch, match=field):
+            BoundGemm(nd, da, db, out, dbias, frozen=other)
