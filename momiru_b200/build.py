@@ -45,18 +45,24 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     if not force and not _stale():
         return LIB_PATH
     os.makedirs(OBJ_DIR, exist_ok=True)
-    jobs = []
+    headers = [os.path.join(CSRC, f) for f in HEADERS] + [os.path.join(HERE, "..", "include", "momiru_gemm.h")]
+    newest_header = max(os.path.getmtime(h) for h in headers if os.path.exists(h))
+    objs, jobs = [], []
     for src in SOURCES:
         obj = os.path.join(OBJ_DIR, os.path.splitext(src)[0] + ".o")
-        cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-c", "-o", obj, os.path.join(CSRC, src)]
+        objs.append(obj)
+        path = os.path.join(CSRC, src)
+        # an object is rebuilt when forced, missing, or older than its unit or any header
+        if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(path), newest_header):
+            continue
+        cmd = [_nvcc(), *NVCC_FLAGS, *(extra or []), "-c", "-o", obj, path]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         jobs.append((obj, subprocess.Popen(cmd)))
     failed = [obj for obj, proc in jobs if proc.wait() != 0]
     if failed:
         raise subprocess.CalledProcessError(1, f"nvcc ({', '.join(os.path.basename(f) for f in failed)})")
-    link = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB_PATH,
-            *[obj for obj, _ in jobs]]
+    link = [_nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB_PATH, *objs]
     if verbose:
         print(" ".join(link), file=sys.stderr)
     subprocess.run(link, check=True)
