@@ -10,7 +10,7 @@ namespace mmr {
 // Recomputes, in the reference's exact order, every output of the tiles the
 // split warps flagged, then clears the bookkeeping for the next run (the last
 // block to finish does it). With nothing flagged every block returns at once.
-__global__ void __launch_bounds__(256) tc_nonfinite_fixup_kernel(const SimtParams sp, const TcParams p) {
+__global__ void __launch_bounds__(256) mmr_tc_nonfinite_fixup_kernel(const SimtParams sp, const TcParams p) {
   __shared__ float As[SIMT_BK][SIMT_BM + 4];
   __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
   __shared__ bool last;

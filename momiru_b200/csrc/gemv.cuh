@@ -75,7 +75,7 @@ __device__ __forceinline__ unsigned long long fma_f32x2(unsigned long long a, un
 }
 
 template <int MT>
-__global__ void __launch_bounds__(GV_THREADS, 2) gemv_cluster_kernel(const __grid_constant__ CUtensorMap tmB,
+__global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const __grid_constant__ CUtensorMap tmB,
                                                                   const GemvParams p) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();

@@ -579,14 +579,14 @@ cudaError_t launch_gemv_mt(const mmr_gemm_handle* h, cudaStream_t s) {
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mmr::gemv_cluster_kernel<MT>, h->tmB, h->gvp);
+  return cudaLaunchKernelEx(&cfg, mmr::mmr_gemv_cluster_kernel<MT>, h->tmB, h->gvp);
 }
 
 template <int MT>
 cudaError_t prepare_gemv_mt(int smem) {
-  cudaError_t e = cudaFuncSetAttribute(mmr::gemv_cluster_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(mmr::mmr_gemv_cluster_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(mmr::gemv_cluster_kernel<MT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+  return cudaFuncSetAttribute(mmr::mmr_gemv_cluster_kernel<MT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
 }
 
 cudaError_t launch_gemv(const mmr_gemm_handle* h, cudaStream_t s) {
@@ -1130,7 +1130,7 @@ struct SignalParams {
 // After this rank's GEMM (whose epilogue fenced its peer stores system-wide):
 // publish `epoch` into every peer's slot for this rank, then wait, bounded,
 // until every peer has published into this rank's array. One warp.
-__global__ void replica_signal_wait_kernel(const SignalParams s) {
+__global__ void mmr_replica_signal_wait_kernel(const SignalParams s) {
   const int t = threadIdx.x;
   const bool peer = t < s.nranks && t != s.rank;
   if (peer) {
@@ -1213,13 +1213,13 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
         e = mmr::tc_launch(h->mode, h->pair, h->a_mn, h->b_mn, mmr::TcShape{h->grid, h->block, h->smem}, s, h->tmA,
                            h->tmB, h->tmC, h->tcp);
         if (e == cudaSuccess && h->mode == 1) {
-          mmr::tc_nonfinite_fixup_kernel<<<h->sms, 256, 0, s>>>(h->sp, h->tcp);
+          mmr::mmr_tc_nonfinite_fixup_kernel<<<h->sms, 256, 0, s>>>(h->sp, h->tcp);
           e = cudaGetLastError();
         }
         break;
       case MMR_FAMILY_GEMV: e = launch_gemv(h, s); break;
       case MMR_FAMILY_SIMT:
-        mmr::simt_gemm_exact_kernel<<<h->grid, h->block, 0, s>>>(h->sp);
+        mmr::mmr_simt_gemm_exact_kernel<<<h->grid, h->block, 0, s>>>(h->sp);
         e = cudaGetLastError();
         break;
       default: return fail(MMR_ERR_UNSUPPORTED_FAMILY, "no kernel bound");
@@ -1234,7 +1234,7 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
     sp.epoch = ++h->epoch;
     sp.err = h->d_err;
     sp.timeout_ns = h->wait_timeout_ns;
-    replica_signal_wait_kernel<<<1, 32, 0, s>>>(sp);
+    mmr_replica_signal_wait_kernel<<<1, 32, 0, s>>>(sp);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) return fail(MMR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
@@ -1324,7 +1324,7 @@ int32_t mmr_gemm_destroy(mmr_gemm_handle* h) {
 }
 
 namespace {
-__global__ void bounded_wait_probe_kernel(int* err, unsigned long long limit_ns) {
+__global__ void mmr_bounded_wait_probe_kernel(int* err, unsigned long long limit_ns) {
   __shared__ uint64_t bar;
   if (threadIdx.x == 0) {
     mmr::mbar_init(&bar, 1);
@@ -1349,7 +1349,7 @@ int32_t mmr_selftest_bounded_wait(int32_t device_ordinal, uint64_t limit_ns) {
   int h = -1;
   cudaError_t e = cudaMemset(d_err, 0, sizeof(int));
   if (e == cudaSuccess) {
-    bounded_wait_probe_kernel<<<1, 32>>>(d_err, limit_ns);
+    mmr_bounded_wait_probe_kernel<<<1, 32>>>(d_err, limit_ns);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
@@ -1467,7 +1467,7 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   cudaError_t ce = mmr::tc_launch(1, false, t.a_mn, t.b_mn, mmr::TcShape{h.grid, h.block, h.smem}, s, h.tmA, h.tmB,
                                   h.tmC, h.tcp);
   if (ce == cudaSuccess) {
-    mmr::tc_nonfinite_fixup_kernel<<<dev->sms, 256, 0, s>>>(h.sp, h.tcp);
+    mmr::mmr_tc_nonfinite_fixup_kernel<<<dev->sms, 256, 0, s>>>(h.sp, h.tcp);
     ce = cudaGetLastError();
   }
   if (ce != cudaSuccess) return fail(MMR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(ce));

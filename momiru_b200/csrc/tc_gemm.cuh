@@ -29,7 +29,7 @@
 // Inputs holding inf or NaN: in 3xTF32 the cross term hi(inf) * lo(b) is
 // inf * 0 = NaN whenever b is exactly representable in TF32, which the
 // reference order never produces. The split warps flag such tiles (a rare
-// path: one atomic per affected stage) and tc_nonfinite_fixup_kernel
+// path: one atomic per affected stage) and mmr_tc_nonfinite_fixup_kernel
 // (fixup.cuh) then recomputes every output of a flagged tile in the
 // reference's exact order.
 #pragma once
@@ -209,7 +209,7 @@ __device__ __forceinline__ void reg_dealloc() {
 
 template <int MODE, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    mmr_tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const TcParams p) {
   using Cfg = TcConfig<MODE>;
   constexpr int S = Cfg::kStages;

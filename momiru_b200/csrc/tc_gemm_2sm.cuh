@@ -1,7 +1,7 @@
 // tc_gemm_2sm.cuh -- f32 GEMM on CTA pairs (tcgen05 cta_group::2), in both
 // numeric modes: MODE 1 = StrictFp32 (3xTF32), MODE 0 = one TF32 pass.
 //
-// Same contract and numerics as tc_gemm_kernel<MODE, ...> (3xTF32 split,
+// Same contract and numerics as mmr_tc_gemm_kernel<MODE, ...> (3xTF32 split,
 // 256-wide K chunks summed with round-to-nearest adds, exact fix-up of tiles
 // with inf/NaN inputs; TF32 keeps one chain per tile segment), but each output
 // tile of 256 x 256 is computed by a cluster of two CTAs on two SMs with one
@@ -138,7 +138,7 @@ struct PairWork {
 
 template <int MODE, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
-    tc_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+    mmr_tc_gemm_2sm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmC, const TcParams p) {
   using Cfg = Tc2Config<MODE>;
   constexpr int S = Cfg::kStages;

@@ -23,9 +23,9 @@ cudaError_t tc_launch_one(const TcShape& sh, cudaStream_t s, const CUtensorMap& 
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_2sm_kernel<MODE, AMN, BMN>, tm_a, tm_b, tm_c, p);
+    return cudaLaunchKernelEx(&cfg, mmr_tc_gemm_2sm_kernel<MODE, AMN, BMN>, tm_a, tm_b, tm_c, p);
   } else {
-    tc_gemm_kernel<MODE, AMN, BMN><<<sh.grid, sh.block, sh.smem, s>>>(tm_a, tm_b, tm_c, p);
+    mmr_tc_gemm_kernel<MODE, AMN, BMN><<<sh.grid, sh.block, sh.smem, s>>>(tm_a, tm_b, tm_c, p);
     return cudaGetLastError();
   }
 }
@@ -41,8 +41,8 @@ cudaError_t tc_prepare_one(int smem) {
   constexpr int epi_regs = PAIR ? Cfg2::kEpiRegs : Cfg1::kEpiRegs;
   constexpr int other_regs = PAIR ? Cfg2::kOtherRegs : Cfg1::kOtherRegs;
   const void* fn;
-  if constexpr (PAIR) fn = reinterpret_cast<const void*>(tc_gemm_2sm_kernel<MODE, AMN, BMN>);
-  else fn = reinterpret_cast<const void*>(tc_gemm_kernel<MODE, AMN, BMN>);
+  if constexpr (PAIR) fn = reinterpret_cast<const void*>(mmr_tc_gemm_2sm_kernel<MODE, AMN, BMN>);
+  else fn = reinterpret_cast<const void*>(mmr_tc_gemm_kernel<MODE, AMN, BMN>);
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   cudaFuncAttributes fa;
