@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--panels", type=int, default=0,
                     help="row panels of the host-buffer e2e path (0 = one per 512 rows, at most 16)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--library-context", action="store_true",
+                    help="also time cuBLAS (torch.matmul, TF32 allowed / strict FP32) on the same operands, "
+                         "outside the timed region, as a library reference point")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--workload", choices=["c3", "c1", "c2", "c4", "c5a", "c5b"], default="c3",
                     help="c3 (default) is the headline line; the others are the remaining configurations, "
@@ -181,6 +184,32 @@ def cpu_baseline_sample(a, b, bias, seconds: float):
             "cpu_model": cpu_model(), "single_thread": single_thread_sample(a, b)}
 
 
+def library_context(fn_by_mode: dict, flops: float, iters: int = 5) -> dict:
+    """cuBLAS on the same operands (torch.matmul), timed with CUDA events after
+    two warm-ups: a reference point from the vendor library, not this path."""
+    import torch
+    out = {}
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        for label, (allow_tf32, fn) in fn_by_mode.items():
+            torch.backends.cuda.matmul.allow_tf32 = allow_tf32
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(iters):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            out[label] = flops / (e0.elapsed_time(e1) / iters * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    out["unit"] = "TFLOP/s"
+    out["what"] = "cuBLAS through torch.matmul on the same device tensors (context only)"
+    return out
+
+
 def dist_init(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -273,19 +302,25 @@ def run_workload(args, rank, world, local):
     def dv(arr):
         return DeviceView.from_host(arr, dev)
 
-    def timed(handles, flops, bytes_, name, cfg, bound):
+    def timed(handles, flops, bytes_, name, cfg, bound, lib=None):
         for _ in range(max(args.warmup, 3)):
             for h in handles:
                 h.replay()
         torch.cuda.synchronize()
+        clocks = ClockSampler(dev)
+        clocks.start()
+        time.sleep(0.3)
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        clocks.active = True
         e0.record(stream)
         for i in range(args.steps):
             handles[i % len(handles)].replay()
         e1.record(stream)
         torch.cuda.synchronize()
+        clocks.active = False
+        clocks.stop()
         ms = e0.elapsed_time(e1) / args.steps
         if world > 1:
             t = torch.tensor([ms], device=f"cuda:{dev}")
@@ -310,7 +345,10 @@ def run_workload(args, rank, world, local):
             "roofline": {"bound": bound, "achieved": per_rank, "peak": peak, "unit": unit, "frac": per_rank / peak,
                          "peak_basis": "measured HBM copy" if bound == "hbm" else
                          f"measured bf16 dense / 2{' / 3' if args.mode == 'strict' else ''}"},
+            "clocks": clocks.summary(),
         })
+        if lib is not None and args.library_context:
+            lines[-1]["library_context"] = library_context(lib, flops / world)
 
     w = args.workload
     if w == "c1":
@@ -327,10 +365,13 @@ def run_workload(args, rank, world, local):
     elif w == "c4":
         x, wt = dv(rng.randn((4096, 4096), 1, 0.02)), dv(rng.randn((4096, 12288), 2, 0.02))
         out = DeviceView.empty((4096, 11008), dev)
+        xt, wtt, ot = x.torch_view(), wt.torch_view(), out.torch_view()
+        lib = {"cublas_tf32": (True, lambda: torch.matmul(xt.t(), wtt[:, :11008], out=ot)),
+               "cublas_fp32": (False, lambda: torch.matmul(xt.t(), wtt[:, :11008], out=ot))}
         timed([BoundGemm(node, x.transpose(), wt.narrow(1, 0, 11008), out, stream=stream.cuda_stream)],
               2.0 * 4096 * 4096 * 11008, 4 * (4096 * 4096 + 2 * 4096 * 11008),
               "C4 strided views 4096x4096x11008 TFLOP/s",
-              {"workload": "c4_xT_4096_wslice_11008", "l2": "inputs 245 MB > L2"}, "tensor")
+              {"workload": "c4_xT_4096_wslice_11008", "l2": "inputs 245 MB > L2"}, "tensor", lib)
     elif w == "c5a":
         b0, b1 = batch_shards(512, world)[rank]
         nb = b1 - b0
@@ -346,10 +387,13 @@ def run_workload(args, rank, world, local):
             at[i:i + j].copy_(blk_a[:j])
             bt[i:i + j].copy_(blk_b[:j])
         out = DeviceView.empty((nb, 1024, 1024), dev)
+        ot = out.torch_view()
+        lib = {"cublas_tf32": (True, lambda: torch.matmul(at, bt, out=ot)),
+               "cublas_fp32": (False, lambda: torch.matmul(at, bt, out=ot))}
         timed([BoundGemm(node, a, b, out, stream=stream.cuda_stream)], 2.0 * 512 * 1024 ** 3,
               4 * 3 * 512 * 1024 ** 2, "C5a batched 512x1024^3 TFLOP/s",
               {"workload": "c5a_batch512_1024^3", "parallelism": f"batch-shard x{world}, no collective",
-               "l2": "inputs 4 GiB > L2"}, "tensor")
+               "l2": "inputs 4 GiB > L2"}, "tensor", lib)
     elif w == "c5b":
         bs = [dv(rng.randn((4096, 4096), 10 + i)) for i in range(4)]
         for m in (1, 4, 16):
@@ -607,6 +651,11 @@ def main():
         "parity": parity,
         "replicas_equal": replicas_equal,
     }
+    if args.library_context and world == 1:
+        cb = torch.empty_like(out_t)
+        line["library_context"] = library_context(
+            {"cublas_tf32": (True, lambda: torch.matmul(a_t, b_t, out=cb)),
+             "cublas_fp32": (False, lambda: torch.matmul(a_t, b_t, out=cb))}, flops_total)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(a_h, b_h, bias_h, args.cpu_seconds)
     g.close()
