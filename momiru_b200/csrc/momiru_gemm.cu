@@ -556,11 +556,12 @@ namespace {
 int32_t encode_tc_maps(mmr_gemm_handle* h, const Plan& p, const TmaLayout& t, int64_t batch, uint32_t bk,
                        uint32_t b_rows = mmr::TC_BN) {
   int32_t e;
-  if (!t.a_mn) e = encode_3d(&h->tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, bk, mmr::TC_BM, "lhs");
+  const uint32_t panel_k = std::min(bk, 32u);  // K-major boxes are one 32-wide (128-byte) panel at most
+  if (!t.a_mn) e = encode_3d(&h->tmA, p.a.base, p.k, p.m, t.a_batched ? batch : 1, p.a.s_r, t.a_sb, panel_k, mmr::TC_BM, "lhs");
   else e = encode_3d(&h->tmA, p.a.base, p.m, p.k, t.a_batched ? batch : 1, p.a.s_c, t.a_sb, 32, bk, "lhs", true);
   if (e) return e;
   if (t.b_mn) e = encode_3d(&h->tmB, p.b.base, p.n, p.k, t.b_batched ? batch : 1, p.b.s_r, t.b_sb, 32, bk, "rhs", true);
-  else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, bk, b_rows, "rhs");
+  else e = encode_3d(&h->tmB, p.b.base, p.k, p.n, t.b_batched ? batch : 1, p.b.s_c, t.b_sb, panel_k, b_rows, "rhs");
   if (e) return e;
   return encode_3d(&h->tmC, p.c.base, p.n, p.m, batch, p.c.s_r, t.c_sb, 32, 32, "out");
 }
@@ -704,12 +705,13 @@ int32_t derive_launch(const Plan& p, const TmaLayout& t, int32_t fam, int sms, L
     if (L.pair) {
       L.smem = L.mode ? mmr::Tc2Config<1>::kSmemBytes : mmr::Tc2Config<0>::kSmemBytes;
       // Fewer tiles than pairs and a long K: split each tile along K over
-      // several pairs, stream-K style, in parts of at least 128 k-blocks. A
-      // split tile costs on the order of 10 us per part over the unsplit
-      // one (measured: 1024^2 x 8192 in 4 parts 319 -> 145 us, but 512^3 in
-      // 4 parts of 8 k-blocks 35 -> 72 us), so short parts do not pay.
+      // several pairs, stream-K style, in parts of at least 2048 K (3xTF32)
+      // or 4096 K (TF32). A split tile costs on the order of 10 us per part
+      // over the unsplit one (measured: 1024^2 x 8192 in 4 parts 319 -> 145
+      // us, but 512^3 in 4 parts of 128 K 35 -> 72 us), so short parts do not pay.
+      const int64_t min_part_k = L.mode ? 2048 : 4096;
       L.split = L.tiles < sms / 2
-                    ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / L.tiles, L.k_blocks / 128))
+                    ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / L.tiles, p.k / min_part_k))
                     : 1;
       L.npairs = std::min<int64_t>(L.tiles, sms / 2) * L.split;
       L.grid = dim3(unsigned(2 * L.npairs));
