@@ -193,10 +193,18 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
       const uint8_t* st = ring + slot * GV_STAGE_BYTES + warp * 4 * (GV_COLS * 4) + lane * 16;
       const int kk0 = s * GV_ROWS + warp * 4;  // row offset within the slice
       const float* a0 = As + kk0 * MT;
+      // This warp's four B rows go to registers and the slot is handed back
+      // before the multiply-adds, so a slot is held for four shared loads,
+      // not for the arithmetic: the whole ring stays in flight from HBM.
+      float4 brow[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) brow[r] = *reinterpret_cast<const float4*>(st + r * (GV_COLS * 4));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         if (k_lo + kk0 + r < k_hi) {
-          const float4 bv = *reinterpret_cast<const float4*>(st + r * (GV_COLS * 4));
+          const float4 bv = brow[r];
           if constexpr (MT >= 2) {
             const unsigned long long bd[4] = {pack_f32x2(bv.x, bv.x), pack_f32x2(bv.y, bv.y),
                                               pack_f32x2(bv.z, bv.z), pack_f32x2(bv.w, bv.w)};
@@ -225,8 +233,6 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
     }
     if constexpr (MT >= 2) {
 #pragma unroll

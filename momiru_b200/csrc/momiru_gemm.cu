@@ -526,6 +526,7 @@ struct mmr_gemm_handle {
   unsigned long long* peer_signal[8] = {};
   unsigned long long* signal = nullptr;
   unsigned long long epoch = 0;
+  CUtensorMap* d_peer_tm = nullptr;  // the peers' replica tensor maps (device memory)
   cudaEvent_t done = nullptr, err_ev = nullptr;
   bool ran = false;
   uint64_t wait_timeout_ns = 2000000000ull;
@@ -1319,6 +1320,7 @@ int32_t mmr_gemm_destroy(mmr_gemm_handle* h) {
     if (h->d_nf) cudaFree(h->d_nf);
     if (h->d_ws) cudaFree(h->d_ws);
     if (h->d_ws_count) cudaFree(h->d_ws_count);
+    if (h->d_peer_tm) cudaFree(h->d_peer_tm);
     if (h->h_err) cudaFreeHost(h->h_err);
   }
   delete h;
@@ -1609,6 +1611,27 @@ int32_t mmr_sharded_gemm_bind(const mmr_sharded_desc* d, mmr_gemm_handle** out) 
   }
   h->tcp.npeers = q;
   h->sp.npeers = q;
+  // One tensor map per peer replica (the local output's geometry at the
+  // peer's address), in device memory: the epilogue stores each finished box
+  // to every replica with TMA stores.
+  if (h->family == MMR_FAMILY_TCGEN05 && q > 0 && !h->plan.empty) {
+    CUtensorMap maps[mmr::kMaxPeers];
+    for (int j = 0; j < q; ++j) {
+      if ((rc = encode_3d(&maps[j], reinterpret_cast<uint64_t>(h->tcp.peer_c[j]), uint64_t(h->tcp.n),
+                          uint64_t(h->tcp.m), uint64_t(h->tcp.batch), h->tcp.c_ld, h->tcp.c_bs, 32, 32,
+                          "peer replica"))) {
+        mmr_gemm_destroy(h);
+        return rc;
+      }
+    }
+    DeviceGuard guard(h->device);
+    if (cudaMalloc(&h->d_peer_tm, sizeof(CUtensorMap) * size_t(q)) != cudaSuccess ||
+        cudaMemcpy(h->d_peer_tm, maps, sizeof(CUtensorMap) * size_t(q), cudaMemcpyHostToDevice) != cudaSuccess) {
+      mmr_gemm_destroy(h);
+      return fail(MMR_ERR_CUDA, "storing the peer tensor maps failed");
+    }
+    h->tcp.peer_tm = h->d_peer_tm;
+  }
   // With replicas to feed and under two rounds of tiles, every tile is split
   // stream-K style: the pairs' ranges then end at staggered points inside
   // tiles, so tiles finish (and their stores leave over NVLink) spread across

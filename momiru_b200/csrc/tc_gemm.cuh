@@ -111,6 +111,11 @@ struct TcParams {
   // peer_c[i] as from c (addresses mapped into this process).
   int npeers;
   float* peer_c[kMaxPeers];
+  // Tensor maps of the peers' replicas (npeers of them, in device memory),
+  // or null: a finished box then leaves for each peer as one TMA store from
+  // the staging buffer (asynchronous: the epilogue warp does not issue the
+  // NVLink stores itself); the ragged right edge keeps plain stores.
+  const CUtensorMap* peer_tm;
   // Stream-K partial sums (CTA-pair kernel): two slots per pair, and arrival
   // counters per split tile and epilogue warp of each CTA (zero between launches).
   float* ws;
@@ -180,9 +185,11 @@ __device__ __forceinline__ void store_box(const TcParams& p, const CUtensorMap* 
   __syncwarp();
   if (lane == 0) {
     tma_store_3d(tmC, buf, col0, row0, bt);
+    if (p.peer_tm != nullptr)
+      for (int q = 0; q < p.npeers; ++q) tma_store_3d(p.peer_tm + q, buf, col0, row0, bt);
     bulk_commit_group();
   }
-  if (p.npeers) store_box_to_peers(p, buf, row0, col0, bt, lane);
+  if (p.npeers && p.peer_tm == nullptr) store_box_to_peers(p, buf, row0, col0, bt, lane);
 }
 
 __device__ __forceinline__ void tc_tile_coords(const TcParams& p, int t, int& mt, int& nt, int& bt) {
@@ -314,7 +321,12 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_group_all();
-    if (p.npeers) __threadfence_system();  // peer stores ordered before the completion signal
+    // peer stores (TMA stores complete with the wait above) ordered before
+    // the completion signal
+    if (p.npeers) {
+      fence_proxy_async_global();
+      __threadfence_system();
+    }
     __syncwarp();
   } else {
     reg_dealloc<Cfg::kOtherRegs>();

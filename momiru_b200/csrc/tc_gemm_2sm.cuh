@@ -324,7 +324,12 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_group_all();
-    if (p.npeers) __threadfence_system();  // peer stores ordered before the completion signal
+    // peer stores (TMA stores complete with the wait above) ordered before
+    // the completion signal
+    if (p.npeers) {
+      fence_proxy_async_global();
+      __threadfence_system();
+    }
     __syncwarp();
   } else {
     reg_dealloc<Cfg::kOtherRegs>();
