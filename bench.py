@@ -303,10 +303,21 @@ def run_workload(args, rank, world, local):
         return DeviceView.from_host(arr, dev)
 
     def timed(handles, flops, bytes_, name, cfg, bound, lib=None):
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0.record(stream)
         for _ in range(max(args.warmup, 3)):
             for h in handles:
                 h.replay()
+        w1.record(stream)
         torch.cuda.synchronize()
+        # a step of a few microseconds: time enough of them that the clock
+        # sampler (100 ms period) sees the timed region
+        est_ms = w0.elapsed_time(w1) / (max(args.warmup, 3) * len(handles))
+        steps = max(args.steps, int(0.6 / max(est_ms * 1e-3, 1e-7)) + 1)
+        if world > 1:
+            t = torch.tensor([steps], device=f"cuda:{dev}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            steps = int(t.item())
         clocks = ClockSampler(dev)
         clocks.start()
         time.sleep(0.3)
@@ -315,13 +326,13 @@ def run_workload(args, rank, world, local):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         clocks.active = True
         e0.record(stream)
-        for i in range(args.steps):
+        for i in range(steps):
             handles[i % len(handles)].replay()
         e1.record(stream)
         torch.cuda.synchronize()
         clocks.active = False
         clocks.stop()
-        ms = e0.elapsed_time(e1) / args.steps
+        ms = e0.elapsed_time(e1) / steps
         if world > 1:
             t = torch.tensor([ms], device=f"cuda:{dev}")
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -336,7 +347,7 @@ def run_workload(args, rank, world, local):
             peak = tf32_peak / 3.0 if args.mode == "strict" else tf32_peak
         per_rank = value / world
         lines.append({
-            "metric": name, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "metric": name, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak" if args.workload == "c5a" and world > 1 else "replicas" if world > 1 else "n/a",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64)", "config": cfg,
@@ -399,7 +410,7 @@ def run_workload(args, rank, world, local):
         for m in (1, 4, 16):
             a = dv(rng.randn((m, 4096), 1))
             outs = [DeviceView.empty((m, 4096), dev) for _ in range(4)]
-            hs = [BoundGemm(MatMulNode(), a, bs[i], outs[i], stream=stream.cuda_stream) for i in range(4)]
+            hs = [BoundGemm(node, a, bs[i], outs[i], stream=stream.cuda_stream) for i in range(4)]
             timed(hs, 2.0 * m * 4096 * 4096, 4 * (m * 4096 + 4096 * 4096 + m * 4096),
                   f"C5b GEMV M={m} N=K=4096 HBM GB/s",
                   {"workload": f"c5b_gemv_m{m}", "l2": "four 64 MiB B copies rotate (256 MiB > L2)"}, "hbm")

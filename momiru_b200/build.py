@@ -14,8 +14,8 @@ CSRC = os.path.join(HERE, "csrc")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libmomiru_gemm.so")
 SOURCES = ["momiru_gemm.cu", "tc_strict_pair.cu", "tc_tf32_pair.cu", "tc_strict_1cta.cu", "tc_tf32_1cta.cu"]
-HEADERS = ["ptx.cuh", "epilogue.cuh", "tc_gemm.cuh", "tc_gemm_2sm.cuh", "simt_gemm.cuh", "gemv.cuh", "fixup.cuh",
-           "tc_launch.h", "tc_launch.cuh"]
+HEADERS = ["ptx.cuh", "epilogue.cuh", "tc_gemm.cuh", "tc_gemm_2sm.cuh", "simt_gemm.cuh", "gemv.cuh", "gemv_tc.cuh", "fixup.cuh",
+           "tc_launch.h", "tc_launch.cuh", "launch.cuh"]
 OBJ_DIR = os.path.join(LIB_DIR, "obj")
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

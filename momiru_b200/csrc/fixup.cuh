@@ -14,6 +14,8 @@ __global__ void __launch_bounds__(256) mmr_tc_nonfinite_fixup_kernel(const SimtP
   __shared__ float As[SIMT_BK][SIMT_BM + 4];
   __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
   __shared__ bool last;
+  griddep_wait();
+  griddep_release();
   const unsigned int count = *reinterpret_cast<volatile unsigned int*>(&p.nf[0]);
   if (count == 0) return;
   const int kSub = (p.tile_m / SIMT_BM) * (TC_BN / SIMT_BN);

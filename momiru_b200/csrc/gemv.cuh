@@ -7,13 +7,17 @@
 //   grid.y  = GV_KSPLIT K-slices; the GV_KSPLIT CTAs of a strip form one
 //             thread-block cluster (dims 1 x GV_KSPLIT x 1)
 //   block   = 8 consumer warps + 1 producer warp
-// The producer thread streams the CTA's B slice through a GV_STAGES-deep
+// The producer thread streams the CTA's B slice through a gv_stages(MT)-deep
 // shared-memory ring with TMA (32 rows x 128 columns, 16 KiB per stage), so
 // the bytes in flight do not depend on registers; the consumer warps take 4
 // rows of each stage (lane = 4 columns) and accumulate M x 4 partial sums.
 // Partials are reduced in a fixed order -- warps through shared memory (the
-// idle ring), then the cluster's CTAs through distributed shared memory -- so
-// results are deterministic, without atomics or a global scratch buffer.
+// idle ring), then the cluster's CTAs: CTA r owns 1/GV_KSPLIT of the strip's
+// outputs, every CTA stores its partial of them into r's receive buffer
+// (slot = its own rank) through distributed shared memory and arrives on r's
+// barrier, and r adds the slots in rank order -- so results are
+// deterministic, without atomics, a global scratch buffer or a cluster-wide
+// barrier at the end.
 // Waits are bounded like the GEMM's.
 #pragma once
 #include <cooperative_groups.h>
@@ -29,7 +33,9 @@ constexpr int GV_THREADS = 32 * (GV_CONSUMER_WARPS + 1);
 constexpr int GV_COLS = 128;
 constexpr int GV_ROWS = 32;                             // B rows per stage
 constexpr int GV_STAGE_BYTES = GV_ROWS * GV_COLS * 4;   // 16 KiB
-constexpr int GV_STAGES = 4;
+// Ring depth: six stages for M <= 4 (the A slice is small), four for larger
+// M, so that two CTAs fit on an SM at every M.
+__host__ __device__ constexpr int gv_stages(int mt) { return mt <= 4 ? 6 : 4; }
 constexpr int GV_KSPLIT = 8;
 constexpr int GV_MAX_M = 16;
 constexpr int GV_MAX_KSLICE = 1024;  // K <= GV_KSPLIT * GV_MAX_KSLICE = 8192
@@ -46,15 +52,16 @@ struct GemvParams {
 };
 
 // Dynamic shared memory: the stage ring (reused afterwards for the per-warp
-// partials [8][MT][128]), the A slice [kslice][MT] (transposed), the CTA partial [MT][128]
-// that cluster peers read, and the ring's barriers.
+// partials [8][MT][128]), the A slice [kslice][MT] (transposed), the receive
+// buffer [GV_KSPLIT][MT * 128 / GV_KSPLIT] that cluster peers write, the
+// ring's barriers and the receive barrier.
 __host__ __device__ constexpr int gemv_ring_bytes(int mt) {
-  return (GV_STAGES * GV_STAGE_BYTES > GV_CONSUMER_WARPS * mt * GV_COLS * 4)
-             ? GV_STAGES * GV_STAGE_BYTES
+  return (gv_stages(mt) * GV_STAGE_BYTES > GV_CONSUMER_WARPS * mt * GV_COLS * 4)
+             ? gv_stages(mt) * GV_STAGE_BYTES
              : GV_CONSUMER_WARPS * mt * GV_COLS * 4;
 }
 __host__ __device__ constexpr int gemv_smem_bytes(int mt, int kslice) {
-  return gemv_ring_bytes(mt) + mt * kslice * 4 + mt * GV_COLS * 4 + 2 * GV_STAGES * 8 + 1024;
+  return gemv_ring_bytes(mt) + mt * kslice * 4 + mt * GV_COLS * 4 + (2 * gv_stages(mt) + 1) * 8 + 1024;
 }
 
 // Packed pairs of f32 (low half = first element) and the sm_100 packed
@@ -79,14 +86,16 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
                                                                   const GemvParams p) {
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
+  constexpr int kStages = gv_stages(MT);
   extern __shared__ uint8_t gv_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gv_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = base;                                                  // [GV_STAGES][32][128] f32
+  uint8_t* ring = base;                                                  // [stages][32][128] f32
   float* red = reinterpret_cast<float*>(base);                           // aliases the ring afterwards
   float* As = reinterpret_cast<float*>(base + gemv_ring_bytes(MT));      // [kslice][MT]
-  float* part = As + MT * p.kslice;                                      // [MT][128]
+  float* part = As + MT * p.kslice;                                      // [GV_KSPLIT][per]
   uint64_t* full = reinterpret_cast<uint64_t*>(part + MT * GV_COLS);
-  uint64_t* empty = full + GV_STAGES;
+  uint64_t* empty = full + kStages;
+  uint64_t* recv = empty + kStages;  // GV_KSPLIT arrivals: every K-slice's partial is in `part`
 
   const int rank = static_cast<int>(cluster.block_rank());  // K-slice index
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -97,13 +106,17 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
   const WaitCtl ctl{p.err, p.timeout_ns};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < GV_STAGES; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], GV_CONSUMER_WARPS);
     }
+    mbar_init(recv, GV_KSPLIT);
     fence_mbar_init();
   }
   __syncthreads();
+  cluster_arrive_release();  // the receive barrier is ready; waited on before the first push
+  griddep_wait();
+  griddep_release();
 
   if (warp == GV_CONSUMER_WARPS) {
     // ---------------------------------------------------------- producer
@@ -111,8 +124,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
       tma_prefetch_desc(&tmB);
       int issued = 0;
       for (int s = 0; s < nstages; ++s) {
-        const int slot = s % GV_STAGES;
-        const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
+        const int slot = s % kStages;
+        const uint32_t phase = static_cast<uint32_t>(s / kStages) & 1u;
         if (!mbar_wait(&empty[slot], phase ^ 1u, ctl, kDevTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&full[slot], GV_STAGE_BYTES);
         tma_load_3d(ring + slot * GV_STAGE_BYTES, &tmB, &full[slot], col0, k_lo + s * GV_ROWS, 0);
@@ -120,9 +133,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
       }
       // Every issued load must land before the ring is reused or the CTA
       // exits (already true on the normal path).
-      for (int s = issued > GV_STAGES ? issued - GV_STAGES : 0; s < issued; ++s) {
-        const uint32_t a = smem_u32(&full[s % GV_STAGES]);
-        const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
+      for (int s = issued > kStages ? issued - kStages : 0; s < issued; ++s) {
+        const uint32_t a = smem_u32(&full[s % kStages]);
+        const uint32_t phase = static_cast<uint32_t>(s / kStages) & 1u;
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(a, phase)) {
           if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
@@ -187,8 +200,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
 #pragma unroll
     for (int i = 0; i < MP; ++i) acc2[i][0] = acc2[i][1] = acc2[i][2] = acc2[i][3] = 0ull;
     for (int s = 0; s < nstages; ++s) {
-      const int slot = s % GV_STAGES;
-      const uint32_t phase = static_cast<uint32_t>(s / GV_STAGES) & 1u;
+      const int slot = s % kStages;
+      const uint32_t phase = static_cast<uint32_t>(s / kStages) & 1u;
       if (!mbar_wait(&full[slot], phase, ctl, kDevTimeoutFull)) break;
       const uint8_t* st = ring + slot * GV_STAGE_BYTES + warp * 4 * (GV_COLS * 4) + lane * 16;
       const int kk0 = s * GV_ROWS + warp * 4;  // row offset within the slice
@@ -250,26 +263,30 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
           make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
   }
   __syncthreads();
-  // CTA partial: fixed warp order 0..7.
+  // CTA partial (fixed warp order 0..7), pushed to its owner: element idx of
+  // the MT x 128 tile belongs to CTA idx / per and lands in slot `rank`.
+  constexpr int per = MT * GV_COLS / GV_KSPLIT;
+  static_assert(MT * GV_COLS % GV_KSPLIT == 0, "owner slices");
+  cluster_wait_acquire();  // every peer's receive barrier is initialised
   for (int idx = threadIdx.x; idx < MT * GV_COLS; idx += GV_THREADS) {
     float sum = 0.0f;
 #pragma unroll
     for (int w = 0; w < GV_CONSUMER_WARPS; ++w) sum += red[w * MT * GV_COLS + idx];
-    part[idx] = sum;
+    cluster.map_shared_rank(part, idx / per)[rank * per + idx % per] = sum;
   }
-  cluster.sync();
+  __syncthreads();
+  if (threadIdx.x < GV_KSPLIT) mbar_arrive_release_cluster(mapa_shared(smem_u32(recv), threadIdx.x));
 
-  // Cluster reduction through DSMEM: CTA `rank` finalises a 1/GV_KSPLIT slice
-  // of this strip's MT x 128 outputs, summing ranks 0..7 in order.
-  const int per = (MT * GV_COLS + GV_KSPLIT - 1) / GV_KSPLIT;
+  // This CTA's share of the strip's outputs: slots 0..GV_KSPLIT-1 in order.
+  // The CTA does not exit before every peer's pushes have landed here.
+  if (!mbar_wait_acquire_cluster(recv, 0u, ctl, kDevTimeoutReduce)) return;
   const bool add_bias = epi_has_bias(p.epilogue);
   const int act = epi_act(p.epilogue);
   for (int j = threadIdx.x; j < per; j += GV_THREADS) {
     const int idx = rank * per + j;
-    if (idx >= MT * GV_COLS) break;
     float sum = 0.0f;
 #pragma unroll
-    for (int q = 0; q < GV_KSPLIT; ++q) sum += cluster.map_shared_rank(part, q)[idx];
+    for (int q = 0; q < GV_KSPLIT; ++q) sum += part[q * per + j];
     const int mm = idx / GV_COLS, cc = col0 + (idx - mm * GV_COLS);
     if (mm < p.m && cc < p.n) {
       if (add_bias) sum = __fadd_rn(sum, p.bias[cc]);
@@ -277,7 +294,6 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
       p.c[mm * p.c_m + cc] = sum;
     }
   }
-  cluster.sync();  // keep this CTA's `part` alive until every peer has read it
 }
 
 }  // namespace mmr

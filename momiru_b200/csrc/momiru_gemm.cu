@@ -21,6 +21,8 @@
 
 #include "../../include/momiru_gemm.h"
 #include "gemv.cuh"
+#include "gemv_tc.cuh"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "fixup.cuh"
 #include "simt_gemm.cuh"
@@ -409,6 +411,21 @@ bool gemv_admission(const Plan& p, const char** why) {
   return true;
 }
 
+// The tensor-core GEMV also streams A through TMA, by 32-wide K panels of its
+// (up to 16) rows: A must be K-contiguous with 16-byte-aligned rows and base.
+// It replaces the CUDA-core GEMV where it is faster (B200, N = K = 4096):
+// TF32 from M = 2 (about 4.6 TB/s at every M; the CUDA-core kernel's time
+// grows with M), StrictFp32 above M = 8, where the CUDA-core kernel's
+// multiply-adds (8 flop per byte of B at M = 16) outlast the split's two
+// tensor-core instructions per k-step.
+constexpr int kGemvTcMinMTf32 = 2, kGemvTcMinMStrict = 9;
+bool gemv_tc_admission(const Plan& p) {
+  if (p.m < (p.math == MMR_MATH_TF32 ? kGemvTcMinMTf32 : kGemvTcMinMStrict)) return false;
+  if (p.a.s_c != 1 || (p.a.base & 15u) != 0) return false;
+  if (p.m > 1 && (p.a.s_r <= 0 || p.a.s_r % 4 != 0)) return false;
+  return true;
+}
+
 // --------------------------------------------------------- TMA encoding --
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -486,6 +503,7 @@ struct Launch {
   int stages = 0, warps = 0, producer_warps = 0, consumer_warps = 0;
   int tmem_columns = 0, tmem_acc_stages = 0;
   int gv_mt = 0, kslice = 0;
+  bool gemv_tc = false;  // GEMV on the tensor cores (swap-AB), else on CUDA cores
   int tensor_maps = 0;
 };
 
@@ -508,6 +526,10 @@ struct mmr_gemm_handle {
   // gemv
   mmr::GemvParams gvp{};
   int gv_mt = 16;
+  // gemv on the tensor cores
+  bool gemv_tc = false;
+  mmr::GemvTcParams gtp{};
+  CUtensorMap tmA_gv;
   // simt
   mmr::SimtParams sp{};
   dim3 grid, block;
@@ -569,19 +591,8 @@ int32_t encode_tc_maps(mmr_gemm_handle* h, const Plan& p, const TmaLayout& t, in
 
 template <int MT>
 cudaError_t launch_gemv_mt(const mmr_gemm_handle* h, cudaStream_t s) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = h->grid;
-  cfg.blockDim = h->block;
-  cfg.dynamicSmemBytes = h->smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = mmr::GV_KSPLIT;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, mmr::mmr_gemv_cluster_kernel<MT>, h->tmB, h->gvp);
+  return mmr::launch_kernel(mmr::mmr_gemv_cluster_kernel<MT>, h->grid, h->block, h->smem, s,
+                            dim3(1, mmr::GV_KSPLIT, 1), h->tmB, h->gvp);
 }
 
 template <int MT>
@@ -589,6 +600,12 @@ cudaError_t prepare_gemv_mt(int smem) {
   cudaError_t e = cudaFuncSetAttribute(mmr::mmr_gemv_cluster_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(mmr::mmr_gemv_cluster_kernel<MT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+}
+
+cudaError_t launch_gemv_tc(const mmr_gemm_handle* h, cudaStream_t s) {
+  const dim3 cluster(1, mmr::GT_KSPLIT, 1);
+  if (h->mode) return mmr::launch_kernel(mmr::mmr_gemv_tc_kernel<1>, h->grid, h->block, h->smem, s, cluster, h->tmB, h->tmA_gv, h->gtp);
+  return mmr::launch_kernel(mmr::mmr_gemv_tc_kernel<0>, h->grid, h->block, h->smem, s, cluster, h->tmB, h->tmA_gv, h->gtp);
 }
 
 cudaError_t launch_gemv(const mmr_gemm_handle* h, cudaStream_t s) {
@@ -733,6 +750,27 @@ int32_t derive_launch(const Plan& p, const TmaLayout& t, int32_t fam, int sms, L
     }
     L.warps = int(L.block.x / 32);
     L.consumer_warps = L.warps - 2;  // epilogue (+ split) warps beside the producer and the MMA issuer
+  } else if (fam == MMR_FAMILY_GEMV && gemv_tc_admission(p)) {
+    // Tensor cores: 128-column strips x GT_KSPLIT K-slices (one cluster per
+    // strip), 32-row stages of B with the matching A panel.
+    L.gemv_tc = true;
+    L.mode = (p.math == MMR_MATH_STRICT_FP32) ? 1 : 0;
+    const int64_t kslice = (p.k + mmr::GT_KSPLIT - 1) / mmr::GT_KSPLIT;
+    L.kslice = int((kslice + mmr::GT_BK - 1) / mmr::GT_BK * mmr::GT_BK);
+    L.smem = mmr::gt_smem_bytes(L.mode);
+    L.grid = dim3(unsigned((p.n + mmr::GT_COLS - 1) / mmr::GT_COLS), mmr::GT_KSPLIT, 1);
+    L.block = dim3(mmr::gt_threads(L.mode));
+    L.cluster_y = mmr::GT_KSPLIT;
+    L.stages = mmr::gt_stages(L.mode);
+    L.warps = int(L.block.x / 32);
+    L.producer_warps = 1;
+    L.consumer_warps = L.warps - 2;
+    L.tile_m = mmr::GT_MN;
+    L.tile_n = mmr::GT_COLS;
+    L.tile_k = mmr::GT_BK;
+    L.tmem_columns = mmr::gt_tmem_cols(L.mode);
+    L.tmem_acc_stages = 2;
+    L.tensor_maps = 2;
   } else if (fam == MMR_FAMILY_GEMV) {
     int kslice = int((p.k + mmr::GV_KSPLIT - 1) / mmr::GV_KSPLIT);
     L.kslice = (kslice + mmr::GV_ROWS - 1) / mmr::GV_ROWS * mmr::GV_ROWS;
@@ -741,7 +779,7 @@ int32_t derive_launch(const Plan& p, const TmaLayout& t, int32_t fam, int sms, L
     L.grid = dim3(unsigned((p.n + mmr::GV_COLS - 1) / mmr::GV_COLS), mmr::GV_KSPLIT, 1);
     L.block = dim3(mmr::GV_THREADS);
     L.cluster_y = mmr::GV_KSPLIT;
-    L.stages = mmr::GV_STAGES;
+    L.stages = mmr::gv_stages(L.gv_mt);
     L.warps = mmr::GV_THREADS / 32;
     L.producer_warps = 1;
     L.consumer_warps = L.warps - 1;
@@ -790,7 +828,7 @@ void to_record(const Launch& L, int32_t math, mmr_launch_record* r) {
   r->producer_warps = L.producer_warps;
   r->consumer_warps = L.consumer_warps;
   const bool tc = L.family == MMR_FAMILY_TCGEN05;
-  r->matrix_acceleration = tc ? MMR_ACCEL_TCGEN05 : MMR_ACCEL_NONE;
+  r->matrix_acceleration = (tc || L.gemv_tc) ? MMR_ACCEL_TCGEN05 : MMR_ACCEL_NONE;
   r->async_copy = L.tensor_maps > 0 ? MMR_ASYNC_COPY_TMA : MMR_ASYNC_COPY_NONE;
   r->tensor_maps = L.tensor_maps;
   if (tc) {
@@ -800,7 +838,7 @@ void to_record(const Launch& L, int32_t math, mmr_launch_record* r) {
     r->persistent_ctas_per_sm = 1;
   } else if (L.family == MMR_FAMILY_GEMV) {
     r->partition = MMR_PARTITION_SPLIT_K;  // K over the CTAs of a cluster, reduced in DSMEM
-    r->split_k = mmr::GV_KSPLIT;
+    r->split_k = L.gemv_tc ? mmr::GT_KSPLIT : mmr::GV_KSPLIT;
     r->use_distributed_shared_memory = 1;
   } else {
     r->partition = MMR_PARTITION_GRID;
@@ -1086,6 +1124,46 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
     h->info.tile_k = L.tile_k;
     h->info.tiles = L.tiles;
     h->info.bytes = algorithmic_bytes(p, t.a_batched, t.b_batched);
+  } else if (fam == MMR_FAMILY_GEMV && L.gemv_tc) {
+    h->gemv_tc = true;
+    h->mode = L.mode;
+    mmr::GemvTcParams& g = h->gtp;
+    g.m = int(p.m);
+    g.n = int(p.n);
+    g.k = int(p.k);
+    g.kslice = L.kslice;
+    g.c = reinterpret_cast<float*>(p.c.base);
+    g.c_m = p.c.s_r;
+    g.bias = reinterpret_cast<const float*>(p.bias);
+    g.epilogue = p.epilogue;
+    g.err = h->d_err;
+    g.timeout_ns = h->wait_timeout_ns;
+    // B by 32 x 32 atoms in the 128-byte swizzle with 32-byte atoms (MN-major
+    // MMA operand); A by 32-wide K panels of its rows (K-major, 128-byte
+    // swizzle); rows of A beyond M arrive as zeros. A one-row A gets any
+    // legal row pitch.
+    const int64_t a_pitch = p.m > 1 ? p.a.s_r : (p.k + 3) / 4 * 4;
+    if (int32_t e = encode_3d(&h->tmB, p.b.base, p.n, p.k, 1, p.b.s_r, 0, 32, mmr::GT_BK, "rhs", true))
+      return cleanup(e);
+    if (int32_t e = encode_3d(&h->tmA_gv, p.a.base, p.k, p.m, 1, a_pitch, 0, mmr::GT_BK, mmr::GT_MN, "lhs"))
+      return cleanup(e);
+    if (h->mode == 1) {
+      if (cudaMalloc(&h->d_nf, 2 * sizeof(unsigned int)) != cudaSuccess ||
+          cudaMemset(h->d_nf, 0, 2 * sizeof(unsigned int)) != cudaSuccess)
+        return cleanup(fail(MMR_ERR_CUDA, "allocating the non-finite flag failed"));
+      g.nf = h->d_nf;
+      fill_simt_params(p, &h->sp);
+    }
+    const void* fn = h->mode ? reinterpret_cast<const void*>(mmr::mmr_gemv_tc_kernel<1>)
+                             : reinterpret_cast<const void*>(mmr::mmr_gemv_tc_kernel<0>);
+    cudaError_t ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, h->smem);
+    if (ce != cudaSuccess) return cleanup(fail(MMR_ERR_CUDA, "cudaFuncSetAttribute(gemv tc): %s", cudaGetErrorString(ce)));
+    h->info.bytes = algorithmic_bytes(p, true, true);
+    h->info.cluster = mmr::GT_KSPLIT;
+    h->info.tile_m = mmr::GT_MN;
+    h->info.tile_n = mmr::GT_COLS;
+    h->info.tile_k = mmr::GT_BK;
+    h->info.stages = mmr::gt_stages(h->mode);
   } else if (fam == MMR_FAMILY_GEMV) {
     mmr::GemvParams& g = h->gvp;
     g.m = int(p.m);
@@ -1215,15 +1293,16 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
       case MMR_FAMILY_TCGEN05:
         e = mmr::tc_launch(h->mode, h->pair, h->a_mn, h->b_mn, mmr::TcShape{h->grid, h->block, h->smem}, s, h->tmA,
                            h->tmB, h->tmC, h->tcp);
-        if (e == cudaSuccess && h->mode == 1) {
-          mmr::mmr_tc_nonfinite_fixup_kernel<<<h->sms, 256, 0, s>>>(h->sp, h->tcp);
-          e = cudaGetLastError();
-        }
+        if (e == cudaSuccess && h->mode == 1)
+          e = mmr::launch_kernel(mmr::mmr_tc_nonfinite_fixup_kernel, dim3(h->sms), dim3(256), 0, s, dim3(1, 1, 1), h->sp, h->tcp);
         break;
-      case MMR_FAMILY_GEMV: e = launch_gemv(h, s); break;
+      case MMR_FAMILY_GEMV:
+        e = h->gemv_tc ? launch_gemv_tc(h, s) : launch_gemv(h, s);
+        if (e == cudaSuccess && h->gemv_tc && h->mode == 1)
+          e = mmr::launch_kernel(mmr::mmr_gemv_tc_fixup_kernel, dim3(h->sms), dim3(256), 0, s, dim3(1, 1, 1), h->sp, h->d_nf);
+        break;
       case MMR_FAMILY_SIMT:
-        mmr::mmr_simt_gemm_exact_kernel<<<h->grid, h->block, 0, s>>>(h->sp);
-        e = cudaGetLastError();
+        e = mmr::launch_kernel(mmr::mmr_simt_gemm_exact_kernel, h->grid, h->block, 0, s, dim3(1, 1, 1), h->sp);
         break;
       default: return fail(MMR_ERR_UNSUPPORTED_FAMILY, "no kernel bound");
     }
@@ -1286,7 +1365,8 @@ int32_t mmr_gemm_quiesce(mmr_gemm_handle* h, uint64_t timeout_ns) {
     cudaMemsetAsync(h->d_err, 0, sizeof(int), h->stream);
     // A run that gave up may leave stream-K arrival counts that nothing reset.
     if (h->d_ws_count) cudaMemsetAsync(h->d_ws_count, 0, h->ws_count_bytes, h->stream);
-    return fail(code == mmr::kDevTimeoutDrain || code <= mmr::kDevTimeoutXform || code == mmr::kDevTimeoutPeer
+    return fail(code == mmr::kDevTimeoutDrain || code <= mmr::kDevTimeoutXform || code == mmr::kDevTimeoutPeer ||
+                        code == mmr::kDevTimeoutReduce
                     ? MMR_ERR_TIMEOUT
                     : MMR_ERR_DEVICE_FAULT_FLAG,
                 "kernel reported device error word %d (a bounded wait expired)", code);
@@ -1470,10 +1550,8 @@ int32_t mmr_gemm_run_noalloc(const mmr_matmul_desc* desc, int32_t* status_out) {
   MMR_CUDA_TRY(cudaMemsetAsync(dev->scratch, 0, (6 + size_t(tiles)) * sizeof(unsigned int), s));
   cudaError_t ce = mmr::tc_launch(1, false, t.a_mn, t.b_mn, mmr::TcShape{h.grid, h.block, h.smem}, s, h.tmA, h.tmB,
                                   h.tmC, h.tcp);
-  if (ce == cudaSuccess) {
-    mmr::mmr_tc_nonfinite_fixup_kernel<<<dev->sms, 256, 0, s>>>(h.sp, h.tcp);
-    ce = cudaGetLastError();
-  }
+  if (ce == cudaSuccess)
+    ce = mmr::launch_kernel(mmr::mmr_tc_nonfinite_fixup_kernel, dim3(dev->sms), dim3(256), 0, s, dim3(1, 1, 1), h.sp, h.tcp);
   if (ce != cudaSuccess) return fail(MMR_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(ce));
   if (status_out)
     MMR_CUDA_TRY(cudaMemcpyAsync(status_out, dev->scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, s));

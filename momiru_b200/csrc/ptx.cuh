@@ -17,7 +17,8 @@ enum : int {
   kDevTimeoutXform = 4,  // MMA gave up waiting for the split operands
   kDevTimeoutDrain = 5,  // teardown gave up draining in-flight copies
   kDevTimeoutProbe = 6,  // the bounded-wait self test expired (expected)
-  kDevTimeoutPeer = 7    // a peer rank never published its replica stores
+  kDevTimeoutPeer = 7,   // a peer rank never published its replica stores
+  kDevTimeoutReduce = 8  // a K-slice CTA's partial sums never arrived
 };
 
 struct WaitCtl {
@@ -135,6 +136,18 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch --
+// Every kernel of the library is launched with programmatic stream
+// serialisation: its CTAs may become resident, initialise their barriers and
+// allocate TMEM while the previous kernel on the stream is still finishing.
+// griddep_wait() blocks until that kernel has completed and its memory is
+// visible; every thread calls it before its first global-memory access (a
+// no-op when the launch had no programmatic predecessor). griddep_release()
+// lets the next such launch start its own prologue; it only schedules CTAs,
+// whose global accesses still wait for this grid to complete.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // -------------------------------------------------------------- tcgen05 --
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
@@ -165,6 +178,18 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem desc], kind::tf32, one CTA. A (M x 8) sits in
+// TMEM K-major: row i in lane i, element k in column a_tmem.col + k.
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05 op this thread issued so far is done.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -186,7 +211,27 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 32 lanes x 16 consecutive 32-bit columns (thread i: lane taddr.lane + i).
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// 32 lanes x 16 consecutive 32-bit columns from registers (thread i: lane
+// taddr.lane + i); a warp reaches only its own quarter of the lanes.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): start
 // address, leading/stride byte offsets (>>4), version 1 at bit 46, layout
@@ -260,6 +305,42 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
 }
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of a cluster barrier, for work in between: every thread of
+// every CTA arrives once and later waits once.
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of CTA-in-cluster address `cluster_addr`, releasing at
+// cluster scope the writes this thread has made or observed (distributed
+// shared-memory stores of the whole CTA after a CTA barrier).
+__device__ __forceinline__ void mbar_arrive_release_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Bounded wait with acquire at cluster scope: the writes released by the
+// arrivals (from any CTA of the cluster) are visible to this thread after it.
+__device__ __forceinline__ bool mbar_wait_acquire_cluster(uint64_t* bar, uint32_t parity, const WaitCtl& ctl,
+                                                          int code) {
+  const uint32_t a = smem_u32(bar);
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if ((it & 31u) == 31u && globaltimer_ns() - t0 > ctl.timeout_ns) {
+      atomicCAS(ctl.err, 0, code);
+      return false;
+    }
+  }
 }
 
 // Two-CTA (cta_group::2) forms: one warp of each CTA of the pair allocates

@@ -12,6 +12,7 @@
 #include <stdint.h>
 
 #include "epilogue.cuh"
+#include "ptx.cuh"
 
 namespace mmr {
 
@@ -109,6 +110,8 @@ __device__ __forceinline__ void simt_block_exact(const SimtParams& p, int m0, in
 __global__ void __launch_bounds__(256) mmr_simt_gemm_exact_kernel(const SimtParams p) {
   __shared__ float As[SIMT_BK][SIMT_BM + 4];
   __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
+  griddep_wait();
+  griddep_release();
   simt_block_exact(p, blockIdx.y * SIMT_BM, blockIdx.x * SIMT_BN, blockIdx.z, As, Bs);
 }
 

@@ -264,6 +264,8 @@ __global__ void __launch_bounds__(TcConfig<MODE>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_release();
   const int n_chunks = (p.k_blocks + p.chunk_kb - 1) / p.chunk_kb;
 
   if (warp < TC_EPI_WARPS) {

@@ -200,6 +200,8 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
   cluster_sync_all();  // barrier inits and both TMEM allocations visible to the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();
+  griddep_release();
 
   if (warp < TC_EPI_WARPS) {
     reg_alloc<Cfg::kEpiRegs>();

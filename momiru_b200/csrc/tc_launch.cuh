@@ -2,6 +2,7 @@
 // (numeric mode x CTA shape) over the four operand-major combinations.
 // Included by exactly one translation unit per family.
 #pragma once
+#include "launch.cuh"
 #include "tc_gemm_2sm.cuh"
 #include "tc_launch.h"
 
@@ -11,22 +12,11 @@ template <int MODE, bool PAIR, bool AMN, bool BMN>
 cudaError_t tc_launch_one(const TcShape& sh, cudaStream_t s, const CUtensorMap& tm_a, const CUtensorMap& tm_b,
                           const CUtensorMap& tm_c, const TcParams& p) {
   if constexpr (PAIR) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = sh.grid;
-    cfg.blockDim = sh.block;
-    cfg.dynamicSmemBytes = sh.smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, mmr_tc_gemm_2sm_kernel<MODE, AMN, BMN>, tm_a, tm_b, tm_c, p);
+    return launch_kernel(mmr_tc_gemm_2sm_kernel<MODE, AMN, BMN>, sh.grid, sh.block, sh.smem, s, dim3(2, 1, 1), tm_a,
+                         tm_b, tm_c, p);
   } else {
-    mmr_tc_gemm_kernel<MODE, AMN, BMN><<<sh.grid, sh.block, sh.smem, s>>>(tm_a, tm_b, tm_c, p);
-    return cudaGetLastError();
+    return launch_kernel(mmr_tc_gemm_kernel<MODE, AMN, BMN>, sh.grid, sh.block, sh.smem, s, dim3(1, 1, 1), tm_a, tm_b,
+                         tm_c, p);
   }
 }
 

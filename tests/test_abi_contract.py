@@ -312,10 +312,30 @@ def test_plan_launch_records_the_bound_launch_for_each_family():
     assert r.async_copy == _abi.ASYNC_COPY_TMA and r.tensor_maps == 3 and r.producer_warps == 1
     assert r.partition == _abi.PARTITION_STREAM_K and r.stream_k_slices > 0 and r.persistent_ctas_per_sm == 1
     check_launch_record(r)
-    g = plan_launch(MatMulNode(), fake((16, 4096), 1), fake((4096, 4096), 2), fake((16, 4096), 3))
-    assert g.family == _abi.FAMILY_GEMV and tuple(g.cluster) == (1, 8, 1) and g.partition == _abi.PARTITION_SPLIT_K
-    assert g.use_distributed_shared_memory == 1 and g.tmem_columns_per_cta == 0
+    tf32 = MatMulNode(math_mode=KernelMathMode.Tf32, accuracy=AccuracyContract.AllowTf32)
+    g = plan_launch(tf32, fake((16, 4096), 1), fake((4096, 4096), 2), fake((16, 4096), 3))
+    # skinny M, TF32: on the tensor cores, 4-CTA clusters over K, 128 x 16 swap-AB tiles, two
+    # interleaved 16-column accumulators per chunk buffer (64 TMEM columns), 11 stages
+    assert g.family == _abi.FAMILY_GEMV and tuple(g.cluster) == (1, 4, 1) and g.partition == _abi.PARTITION_SPLIT_K
+    assert g.use_distributed_shared_memory == 1 and g.matrix_acceleration == _abi.ACCEL_TCGEN05
+    assert (g.tile_m, g.tile_n, g.tile_k, g.tmem_columns_per_cta, g.tensor_maps) == (16, 128, 32, 64, 2)
+    assert g.pipeline_stages == 11
     check_launch_record(g)
+    # StrictFp32 at M = 16: tensor cores too, with lo(B) in TMEM (256 columns), 4 stages
+    s = plan_launch(MatMulNode(), fake((16, 4096), 1), fake((4096, 4096), 2), fake((16, 4096), 3))
+    assert s.family == _abi.FAMILY_GEMV and tuple(s.cluster) == (1, 4, 1) and s.tmem_columns_per_cta == 256
+    assert s.matrix_acceleration == _abi.ACCEL_TCGEN05 and s.pipeline_stages == 4
+    check_launch_record(s)
+    # StrictFp32 at M <= 8, TF32 at M = 1, or an A without a 16-byte row pitch: the CUDA-core GEMV
+    # (8-CTA clusters, no TMEM)
+    for node, m in ((MatMulNode(), 8), (MatMulNode(), 1), (tf32, 1)):
+        c = plan_launch(node, fake((m, 4096), 1), fake((4096, 4096), 2), fake((m, 4096), 3))
+        assert c.family == _abi.FAMILY_GEMV and tuple(c.cluster) == (1, 8, 1) and c.tmem_columns_per_cta == 0
+        assert c.matrix_acceleration == _abi.ACCEL_NONE
+        check_launch_record(c)
+    c = plan_launch(tf32, fake((5, 4095), 1, pad_cols=4097), fake((4095, 4096), 2), fake((5, 4096), 3))
+    assert c.family == _abi.FAMILY_GEMV and tuple(c.cluster) == (1, 8, 1) and c.tmem_columns_per_cta == 0
+    check_launch_record(c)
     e = plan_launch(MatMulNode(math_mode=KernelMathMode.Exact, accuracy=AccuracyContract.Exact), fake((100, 64), 1),
                     fake((64, 200), 2), fake((100, 200), 3))
     assert e.family == _abi.FAMILY_SIMT and e.async_copy == _abi.ASYNC_COPY_NONE and tuple(e.grid) == (4, 2, 1)
