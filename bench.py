@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--workload", choices=["c3", "c1", "c2", "c4", "c5a", "c5b"], default="c3",
                     help="c3 (default) is the headline line; the others are the remaining configurations, "
                          "measured the same way and reported one JSON line each")
+    ap.add_argument("--gemv-m", type=int, choices=[1, 4, 16], default=0,
+                    help="c5b: time only this M (default: M = 1, 4 and 16)")
     return ap.parse_args()
 
 
@@ -407,7 +409,7 @@ def run_workload(args, rank, world, local):
                "l2": "inputs 4 GiB > L2"}, "tensor", lib)
     elif w == "c5b":
         bs = [dv(rng.randn((4096, 4096), 10 + i)) for i in range(4)]
-        for m in (1, 4, 16):
+        for m in ((args.gemv_m,) if args.gemv_m else (1, 4, 16)):
             a = dv(rng.randn((m, 4096), 1))
             outs = [DeviceView.empty((m, 4096), dev) for _ in range(4)]
             hs = [BoundGemm(node, a, bs[i], outs[i], stream=stream.cuda_stream) for i in range(4)]
