@@ -723,11 +723,13 @@ int32_t derive_launch(const Plan& p, const TmaLayout& t, int32_t fam, int sms, L
     if (L.pair) {
       L.smem = L.mode ? mmr::Tc2Config<1>::kSmemBytes : mmr::Tc2Config<0>::kSmemBytes;
       // Fewer tiles than pairs and a long K: split each tile along K over
-      // several pairs, stream-K style, in parts of at least 2048 K (3xTF32)
-      // or 4096 K (TF32). A split tile costs on the order of 10 us per part
-      // over the unsplit one (measured: 1024^2 x 8192 in 4 parts 319 -> 145
-      // us, but 512^3 in 4 parts of 128 K 35 -> 72 us), so short parts do not pay.
-      const int64_t min_part_k = L.mode ? 2048 : 4096;
+      // several pairs, stream-K style, in parts of at least 512 K (3xTF32)
+      // or 1024 K (TF32). Measured on B200 with parts of 2048 / 512 / 256 /
+      // 64 K (3xTF32): 512^2 x 4096 76 / 40.5 / 44.2 / 46.1 us, 256^2 x
+      // 16384 82 / 61 / 83 / 100 us; TF32 1024^2 x 8192 60 / 45 us at
+      // 4096 / 1024 K. Each part parks a 256 KB partial tile in L2 and the
+      // last one reads them all back, which is what shorter parts lose on.
+      const int64_t min_part_k = L.mode ? 512 : 1024;
       L.split = L.tiles < sms / 2
                     ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / L.tiles, p.k / min_part_k))
                     : 1;

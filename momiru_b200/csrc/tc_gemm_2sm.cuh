@@ -214,8 +214,10 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
     const int act = epi_act(p.epilogue);
     const bool relu = act == ACT_RELU;
     const uint32_t acc_empty_leader0 = mapa_shared(smem_u32(&acc_empty[0]), 0);
-    // This thread's 128 columns of its row inside a partial-sum slot.
-    const int ws_off = static_cast<int>(rank) * 128 * TC_BN + (quarter * 32 + lane) * TC_BN + half * 128;
+    // This warp's 32 rows x 128 columns inside a partial-sum slot: 16 KiB of
+    // its own, float4 q of lane l at (q * 32 + l), so that each store or load
+    // instruction of the warp covers 512 contiguous bytes.
+    const int ws_warp = ((static_cast<int>(rank) * 4 + quarter) * 2 + half) * (32 * 128);
     float sum[128];
 
     // Applies the epilogue (bias, activation) to sum[] and stores this
@@ -245,9 +247,10 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
       }
     };
     auto save_partial = [&](float* slot) {
-      float4* dst = reinterpret_cast<float4*>(slot + ws_off);
+      float4* dst = reinterpret_cast<float4*>(slot + ws_warp) + lane;
 #pragma unroll
-      for (int q = 0; q < 32; ++q) dst[q] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
+      for (int q = 0; q < 32; ++q)
+        dst[q * 32] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
     };
 
     bool ok = true;
@@ -308,11 +311,11 @@ __global__ void __launch_bounds__(Tc2Config<MODE>::kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) sum[hh * 64 + i] = 0.0f;
         for (int q = q0; q <= q1; ++q) {
-          const float4* src =
-              reinterpret_cast<const float4*>(p.ws + (2 * q + (q == q1 ? 0 : 1)) * kSkSlotFloats + ws_off) + hh * 16;
+          const float4* src = reinterpret_cast<const float4*>(p.ws + (2 * q + (q == q1 ? 0 : 1)) * kSkSlotFloats +
+                                                              ws_warp) + (hh * 16) * 32 + lane;
           float4 v[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = __ldcg(src + i);
+          for (int i = 0; i < 16; ++i) v[i] = __ldcg(src + i * 32);
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             float* d = sum + hh * 64 + 4 * i;
