@@ -186,9 +186,11 @@ def cpu_baseline_sample(a, b, bias, seconds: float):
             "cpu_model": cpu_model(), "single_thread": single_thread_sample(a, b)}
 
 
-def library_context(fn_by_mode: dict, flops: float, iters: int = 5) -> dict:
+def library_context(fn_by_mode: dict, flops: float, iters: int) -> dict:
     """cuBLAS on the same operands (torch.matmul), timed with CUDA events after
-    two warm-ups: a reference point from the vendor library, not this path."""
+    two warm-ups over as many back-to-back calls as the measured region had
+    steps (a long run settles at the power cap, a short burst does not): a
+    reference point from the vendor library, not this path."""
     import torch
     out = {}
     prev = torch.backends.cuda.matmul.allow_tf32
@@ -208,6 +210,7 @@ def library_context(fn_by_mode: dict, flops: float, iters: int = 5) -> dict:
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
     out["unit"] = "TFLOP/s"
+    out["iters"] = iters
     out["what"] = "cuBLAS through torch.matmul on the same device tensors (context only)"
     return out
 
@@ -361,7 +364,7 @@ def run_workload(args, rank, world, local):
             "clocks": clocks.summary(),
         })
         if lib is not None and args.library_context:
-            lines[-1]["library_context"] = library_context(lib, flops / world)
+            lines[-1]["library_context"] = library_context(lib, flops / world, steps)
 
     w = args.workload
     if w == "c1":
@@ -668,7 +671,7 @@ def main():
         cb = torch.empty_like(out_t)
         line["library_context"] = library_context(
             {"cublas_tf32": (True, lambda: torch.matmul(a_t, b_t, out=cb)),
-             "cublas_fp32": (False, lambda: torch.matmul(a_t, b_t, out=cb))}, flops_total)
+             "cublas_fp32": (False, lambda: torch.matmul(a_t, b_t, out=cb))}, flops_total, args.steps)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_sample(a_h, b_h, bias_h, args.cpu_seconds)
     g.close()
