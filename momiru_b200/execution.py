@@ -343,17 +343,6 @@ class HostGemm:
             pass
 
 
-class GpuGemmBackend:
-    """The Backend entry point for GPU MatMul nodes (runtime.rs:954-988)."""
-
-    validate = staticmethod(validate)
-
-    @staticmethod
-    def bind(node: MatMulNode, lhs: DeviceView, rhs: DeviceView, out: DeviceView, bias: DeviceView | None = None,
-             stream: int | None = None) -> BoundGemm:
-        return BoundGemm(node, lhs, rhs, out, bias, stream)
-
-
 def output_dims(node: MatMulNode, lhs: DeviceView, rhs: DeviceView) -> tuple:
     """Output shape by the MatMul contract (validation.rs:2300-2398)."""
     lv, rv = lhs.rank == 1, rhs.rank == 1

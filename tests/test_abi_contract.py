@@ -28,7 +28,8 @@ def fake(dims, slot, pad_cols=None):
 
 
 def test_library_exports_every_declared_symbol(cuda_lib):
-    header = open(os.path.join(ROOT, "include", "momiru_gemm.h")).read()
+    with open(os.path.join(ROOT, "include", "momiru_gemm.h")) as f:
+        header = f.read()
     declared = set(re.findall(r"MMR_API\s+(?:int32_t|const char \*)\s*(mmr_\w+)\s*\(", header))
     assert declared, "no declarations parsed"
     assert declared == set(_abi.EXPORTED)

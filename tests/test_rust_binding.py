@@ -11,8 +11,13 @@ import pytest
 from momiru_b200 import _abi
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-FFI = open(os.path.join(ROOT, "rust", "src", "gpu_gemm", "ffi.rs")).read()
-HEADER = open(os.path.join(ROOT, "include", "momiru_gemm.h")).read()
+def _read(*parts):
+    with open(os.path.join(ROOT, *parts)) as f:
+        return f.read()
+
+
+FFI = _read("rust", "src", "gpu_gemm", "ffi.rs")
+HEADER = _read("include", "momiru_gemm.h")
 
 
 def header_constants():
