@@ -555,12 +555,16 @@ def main():
     # host memory, the result copied back, all inside the timed region. On one
     # GPU that is the host-buffer entry (mmr_gemm_bind_host: rhs and bias in,
     # then lhs by row panels overlapped with the panels' GEMMs and the copies
-    # out); across ranks each rank copies its inputs in and rank 0 copies the
-    # replicated result out.
+    # out). Across ranks every byte of the inputs and of the result crosses
+    # PCIe once, spread over the ranks' links: each rank copies in its row slab
+    # of A (the slabs are then all-gathered over NVLink, since every rank's
+    # GEMM reads all of A) and its column block of B and bias, and copies out
+    # its column block of the replicated result; the ranks' host blocks
+    # together hold C. h2d/d2h bytes are whole-job totals.
     a_pin = torch.from_numpy(a_h).pin_memory()
     b_pin = torch.from_numpy(b_h).pin_memory()
     bias_pin = torch.from_numpy(bias_h).pin_memory()
-    c_pin = torch.empty(tuple(out_t.shape), dtype=torch.float32).pin_memory() if rank == 0 else None
+    c_pin = torch.empty(tuple(out_t.shape), dtype=torch.float32).pin_memory() if world == 1 else None
     h2d = (a_pin.numel() + b_pin.numel() + bias_pin.numel()) * 4
     d2h = out_t.numel() * 4
     e2e_path = "torch copies + replicated GEMM"
@@ -573,25 +577,29 @@ def main():
         def e2e_step():
             hg.replay()
     else:
-        # Each rank's GEMM reads all of A but only its column block of B and
-        # bias, so that is what it copies in (B's block as one pitched copy);
-        # rank 0 copies the replicated result out.
         from cuda.bindings import runtime as cudart
-        h2d = (a_pin.numel() + n * ncols + ncols) * 4
-        e2e_path = "A + this rank's B/bias column block in, replicated GEMM, rank 0 copies C out"
+        r0, r1 = rank * n // world, (rank + 1) * n // world
+        a_slab = torch.empty((r1 - r0, n), dtype=torch.float32, device=dev)
+        c_block = torch.empty((n, ncols), dtype=torch.float32).pin_memory()
+        e2e_path = ("each rank: its A row slab in, A all-gathered over NVLink, its B/bias column block in, "
+                    "replicated GEMM, its C column block out")
 
-        def e2e_step():
-            a_t.copy_(a_pin, non_blocking=True)
-            if ncols:
-                err, = cudart.cudaMemcpy2DAsync(b_t.data_ptr() + 4 * c0, 4 * n, b_pin.data_ptr() + 4 * c0, 4 * n,
-                                                4 * ncols, n, cudart.cudaMemcpyKind.cudaMemcpyHostToDevice,
-                                                stream.cuda_stream)
+        def copy2d(dst, dpitch, src, spitch, width, rows, kind):
+            if width and rows:
+                err, = cudart.cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, kind, stream.cuda_stream)
                 if err != cudart.cudaError_t.cudaSuccess:
                     raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
+
+        def e2e_step():
+            a_slab.copy_(a_pin[r0:r1], non_blocking=True)
+            dist.all_gather_into_tensor(a_t, a_slab)
+            copy2d(b_t.data_ptr() + 4 * c0, 4 * n, b_pin.data_ptr() + 4 * c0, 4 * n, 4 * ncols, n,
+                   cudart.cudaMemcpyKind.cudaMemcpyHostToDevice)
+            if ncols:
                 bias_t[c0:c1].copy_(bias_pin[c0:c1], non_blocking=True)
             g.replay()
-            if rank == 0:
-                c_pin.copy_(out_t, non_blocking=True)
+            copy2d(c_block.data_ptr(), 4 * ncols, out_t.data_ptr() + 4 * c0, 4 * n, 4 * ncols, n,
+                   cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -627,6 +635,12 @@ def main():
         everyone = [torch.empty_like(digest) for _ in range(world)]
         dist.all_gather(everyone, digest)
         replicas_equal = all(bool(torch.equal(d, everyone[0])) for d in everyone)
+    # the host copy of the result is this rank's column block of the replica
+    e2e_host_ok = None
+    if world > 1:
+        bad = torch.tensor([0 if torch.equal(c_block, out_t[:, c0:c1].cpu()) else 1], device=dev)
+        dist.all_reduce(bad, op=dist.ReduceOp.SUM)
+        e2e_host_ok = int(bad.item()) == 0
     parity = None
     if rank == 0:
         parity = sampled_parity(out_t, a_h, b_h, bias_h, args.mode)
@@ -666,6 +680,7 @@ def main():
         "clocks": clocks.summary(),
         "parity": parity,
         "replicas_equal": replicas_equal,
+        "e2e_host_result_equal": e2e_host_ok,
     }
     if args.library_context and world == 1:
         cb = torch.empty_like(out_t)
