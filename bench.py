@@ -590,9 +590,14 @@ def main():
                 if err != cudart.cudaError_t.cudaSuccess:
                     raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
 
+        even = n % world == 0  # equal slabs for the all-gather; otherwise every rank copies all of A
+
         def e2e_step():
-            a_slab.copy_(a_pin[r0:r1], non_blocking=True)
-            dist.all_gather_into_tensor(a_t, a_slab)
+            if even:
+                a_slab.copy_(a_pin[r0:r1], non_blocking=True)
+                dist.all_gather_into_tensor(a_t, a_slab)
+            else:
+                a_t.copy_(a_pin, non_blocking=True)
             copy2d(b_t.data_ptr() + 4 * c0, 4 * n, b_pin.data_ptr() + 4 * c0, 4 * n, 4 * ncols, n,
                    cudart.cudaMemcpyKind.cudaMemcpyHostToDevice)
             if ncols:
