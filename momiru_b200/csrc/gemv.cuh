@@ -1,7 +1,7 @@
 // gemv.cuh -- skinny-M (M <= 16) f32 matmul that streams B from HBM once.
 //
 // y[m, n] = epilogue(sum_k A[m, k] * B[k, n]) for a row-major B. The work is
-// HBM-bound (B is read exactly once, 4*K*N bytes), so the kernel is judged in
+// HBM-bound (B is read exactly once, 4*K*N bytes), so the kernel is measured in
 // GB/s. Launch:
 //   grid.x  = ceil(N / 128) column strips of 128 columns
 //   grid.y  = GV_KSPLIT K-slices; the GV_KSPLIT CTAs of a strip form one

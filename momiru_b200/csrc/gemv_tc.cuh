@@ -1,7 +1,7 @@
 // gemv_tc.cuh -- skinny-M (M <= 16) f32 matmul on the tensor cores, swap-AB.
 //
 // y[m, n] = epilogue(sum_k A[m, k] * B[k, n]) for a row-major B that is read
-// from HBM exactly once (the GEMV family's work; judged in GB/s). The
+// from HBM exactly once (the GEMV family's work; measured in GB/s). The
 // CUDA-core GEMV (gemv.cuh) spends its time in the packed multiply-adds at
 // M = 16 (8 flop per byte of B); here the tensor core does them:
 //   D[n, m] (+)= B^T[n, k] * A^T[k, m]
