@@ -5,9 +5,9 @@ oracle (the restated reference CPU GEMM), through the C ABI.
        Frobenius) and TF32 (<= 2e-3); the oracle runs once on every host core
        (the reference order is per element, so row-sharding it is bit-exact).
   C5a  the real batch of 512 x 1024^3: 16 batch entries spread over the whole
-       range (first and last included), each in full.
+       range (first and last included), each in full; both modes.
   C4   4096 x 4096 x 11008 through the transposed-lhs and column-slice views:
-       512 rows spread over the output.
+       512 rows spread over the output; both modes.
 """
 import os
 
@@ -69,14 +69,16 @@ def test_c5a_real_batch_512_sampled_entries(oracle):
     b = oracle.randu(bsz * n * n, 2).reshape(bsz, n, n)
     da, db = DeviceView.from_host(a), DeviceView.from_host(b)
     out = DeviceView.empty((bsz, n, n))
-    node = MatMulNode(math_mode=KernelMathMode.StrictFp32)
-    bound_run(node, da, db, out)
     picks = sorted(set(np.linspace(0, bsz - 1, 16).astype(int).tolist()))
-    got = out.torch_view()[picks].cpu().numpy()
-    torch.cuda.synchronize()
-    for j, i in enumerate(picks):
-        ref = oracle.matmul(a[i], b[i], nthreads=CORES)
-        assert rel_frob(got[j], ref) <= STRICT_TOL, i
+    refs = [oracle.matmul(a[i], b[i], nthreads=CORES) for i in picks]
+    for node, tol in ((MatMulNode(math_mode=KernelMathMode.StrictFp32), STRICT_TOL),
+                      (MatMulNode(math_mode=KernelMathMode.Tf32, accuracy=execution.AccuracyContract.AllowTf32),
+                       TF32_TOL)):
+        bound_run(node, da, db, out)
+        got = out.torch_view()[picks].cpu().numpy()
+        torch.cuda.synchronize()
+        for j, i in enumerate(picks):
+            assert rel_frob(got[j], refs[j]) <= tol, (node.math_mode, i)
 
 
 def test_c4_full_size_512_rows(oracle):
@@ -86,7 +88,10 @@ def test_c4_full_size_512_rows(oracle):
     rows = np.unique(np.linspace(0, m - 1, 512).astype(np.int64))
     ref = oracle.matmul(x.T, w[:, :n], rows=rows, nthreads=CORES)
     out = DeviceView.empty((m, n))
-    bound_run(MatMulNode(math_mode=KernelMathMode.StrictFp32), DeviceView.from_host(x).transpose(),
-              DeviceView.from_host(w).narrow(1, 0, n), out)
-    got = out.torch_view()[rows.tolist()].cpu().numpy()
-    assert rel_frob(got, ref) <= STRICT_TOL
+    dx, dw = DeviceView.from_host(x).transpose(), DeviceView.from_host(w).narrow(1, 0, n)
+    for node, tol in ((MatMulNode(math_mode=KernelMathMode.StrictFp32), STRICT_TOL),
+                      (MatMulNode(math_mode=KernelMathMode.Tf32, accuracy=execution.AccuracyContract.AllowTf32),
+                       TF32_TOL)):
+        bound_run(node, dx, dw, out)
+        got = out.torch_view()[rows.tolist()].cpu().numpy()
+        assert rel_frob(got, ref) <= tol, node.math_mode
