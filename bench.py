@@ -79,7 +79,8 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampled every 100 ms while `active` is set."""
+    """nvidia-smi sampled every 25 ms while `active` is set (a short timed
+    region at several GPUs still gets a few samples)."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -94,7 +95,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "25",
                  "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -316,7 +317,7 @@ def run_workload(args, rank, world, local):
         w1.record(stream)
         torch.cuda.synchronize()
         # a step of a few microseconds: time enough of them that the clock
-        # sampler (100 ms period) sees the timed region
+        # sampler (25 ms period) sees the timed region
         est_ms = w0.elapsed_time(w1) / (max(args.warmup, 3) * len(handles))
         steps = max(args.steps, int(0.6 / max(est_ms * 1e-3, 1e-7)) + 1)
         if world > 1:
