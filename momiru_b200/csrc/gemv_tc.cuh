@@ -31,16 +31,17 @@
 // StrictFp32 the panel's low parts follow it in the same layout.
 // K is accumulated in chunks in two TMEM buffers and the chunks are summed
 // with round-to-nearest adds (the tensor core's own accumulation is not RN),
-// as in the GEMM. Inputs with inf/NaN: the split warps raise a flag and
-// mmr_gemv_tc_fixup_kernel recomputes the whole output in the reference's
-// exact order. Every wait is bounded.
+// as in the GEMM. Inputs with inf/NaN (StrictFp32): the split warps raise a
+// flag in their CTA, the CTAs of a strip pass it to one another with their
+// partial sums (together they see all of A and the strip's columns of B), and
+// then each owner computes its outputs again in the reference's exact order
+// instead of adding the partials. Every wait is bounded.
 #pragma once
 #include <cooperative_groups.h>
 #include <stdint.h>
 
 #include "epilogue.cuh"
 #include "ptx.cuh"
-#include "simt_gemm.cuh"
 
 namespace mmr {
 
@@ -97,7 +98,7 @@ constexpr int GT_BAR_BYTES = 512;
 __host__ __device__ constexpr int gt_smem_bytes(int mode) {
   return gt_stages(mode) * gt_stage_bytes(mode) + GT_PART_BYTES + GT_BAR_BYTES + 1024;
 }
-static_assert((3 * 11 + 2 * GT_ACC_BUFS + 2) * 8 + 4 <= GT_BAR_BYTES, "barrier area");
+static_assert((3 * 11 + 2 * GT_ACC_BUFS + 2) * 8 + 8 <= GT_BAR_BYTES, "barrier area");
 static_assert(gt_smem_bytes(0) <= 227 * 1024 && gt_smem_bytes(1) <= 227 * 1024, "shared memory");
 
 struct GemvTcParams {
@@ -108,7 +109,10 @@ struct GemvTcParams {
   int epilogue;
   int* err;
   unsigned long long timeout_ns;
-  unsigned int* nf;           // StrictFp32: [0] inf/NaN seen, [1] fix-up blocks done
+  // StrictFp32: the operands again, for the exact recompute of a strip
+  // whose inputs hold inf or NaN (A is K-contiguous).
+  const float* a; long long a_m;
+  const float* b; long long b_k;
 };
 
 // MMA instruction descriptor geometry: B tile = MN-major A operand (32-column
@@ -140,6 +144,7 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
   uint64_t* drain = acc_full + 2 * kAcc;
   uint64_t* recv = drain + 1;        // GT_KSPLIT arrivals: every K-slice's partial is in `part`
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv + 1);
+  uint32_t* nonfinite_seen = tmem_slot + 1;  // StrictFp32: an input of this strip held inf/NaN
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rank = static_cast<int>(cluster.block_rank());  // K-slice index
@@ -162,6 +167,7 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
     }
     mbar_init(drain, 1);
     mbar_init(recv, GT_KSPLIT);
+    *nonfinite_seen = 0u;
     fence_mbar_init();
   }
   if (warp == GT_PRODUCER_WARP && lane == 0) {
@@ -351,7 +357,7 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&split_done[slot]);
     }
-    if (__any_sync(0xffffffffu, nonfinite) && lane == 0 && p.nf != nullptr) atomicOr(&p.nf[0], 1u);
+    if (__any_sync(0xffffffffu, nonfinite) && lane == 0) atomicOr(nonfinite_seen, 1u);
   }
 
   tc_fence_before();
@@ -378,44 +384,35 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
       cluster.map_shared_rank(part, i / kRowsPer)[rank * kPer + (i % kRowsPer) * GT_COLS + n] = sum[i];
   }
   __syncthreads();
-  if (threadIdx.x < GT_KSPLIT) mbar_arrive_release_cluster(mapa_shared(smem_u32(recv), threadIdx.x));
+  if (threadIdx.x < GT_KSPLIT) {
+    // this CTA's inf/NaN flag travels with its partials (the arrive releases both)
+    if (MODE && *nonfinite_seen) atomicOr(cluster.map_shared_rank(nonfinite_seen, threadIdx.x), 1u);
+    mbar_arrive_release_cluster(mapa_shared(smem_u32(recv), threadIdx.x));
+  }
   if (!mbar_wait_acquire_cluster(recv, 0u, ctl, kDevTimeoutReduce)) return;
   const bool add_bias = epi_has_bias(p.epilogue);
   const int act = epi_act(p.epilogue);
+  // StrictFp32 with inf/NaN in the strip's inputs: the split products can
+  // differ from the reference (inf * 0 = NaN in a cross term), so each owned
+  // output is computed again in the reference's order, s = s + a * b with
+  // the product and the sum rounded, k increasing.
+  const bool exact = MODE && *reinterpret_cast<volatile uint32_t*>(nonfinite_seen) != 0u;
   for (int j = threadIdx.x; j < kPer; j += blockDim.x) {
     const int idx = rank * kPer + j;
-    float v = 0.0f;
-#pragma unroll
-    for (int q = 0; q < GT_KSPLIT; ++q) v = __fadd_rn(v, part[q * kPer + j]);
     const int mm = idx / GT_COLS, cc = col0 + (idx - mm * GT_COLS);
+    float v = 0.0f;
+    if (exact) {
+      if (mm >= p.m || cc >= p.n) continue;
+      const float* a = p.a + mm * p.a_m;
+      for (int kk = 0; kk < p.k; ++kk) v = __fadd_rn(v, __fmul_rn(a[kk], p.b[kk * p.b_k + cc]));
+    } else {
+#pragma unroll
+      for (int q = 0; q < GT_KSPLIT; ++q) v = __fadd_rn(v, part[q * kPer + j]);
+    }
     if (mm < p.m && cc < p.n) {
       if (add_bias) v = __fadd_rn(v, p.bias[cc]);
       p.c[mm * p.c_m + cc] = act_apply(act, v);
     }
-  }
-}
-
-// StrictFp32 only: when an input held inf or NaN, the split products can
-// differ from the reference (inf * 0 = NaN in a cross term), so the whole
-// output is recomputed in the reference's exact order; the last block to
-// finish clears the flag for the next run. With no flag every block returns.
-__global__ void __launch_bounds__(256) mmr_gemv_tc_fixup_kernel(const SimtParams sp, unsigned int* nf) {
-  __shared__ float As[SIMT_BK][SIMT_BM + 4];
-  __shared__ float Bs[SIMT_BK][SIMT_BN + 4];
-  __shared__ bool last;
-  griddep_wait();
-  griddep_release();
-  if (*reinterpret_cast<volatile unsigned int*>(&nf[0]) == 0u) return;
-  const int bn = (sp.n + SIMT_BN - 1) / SIMT_BN, bm = (sp.m + SIMT_BM - 1) / SIMT_BM;
-  for (int w = blockIdx.x; w < bn * bm; w += gridDim.x) simt_block_exact(sp, (w / bn) * SIMT_BM, (w % bn) * SIMT_BN, 0, As, Bs);
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = (atomicAdd(&nf[1], 1u) == gridDim.x - 1);
-  __syncthreads();
-  if (last && threadIdx.x == 0) {
-    __threadfence();
-    nf[0] = 0u;
-    nf[1] = 0u;
   }
 }
 

@@ -1149,13 +1149,10 @@ int32_t mmr_gemm_bind(const mmr_matmul_desc* desc, mmr_gemm_handle** out) {
       return cleanup(e);
     if (int32_t e = encode_3d(&h->tmA_gv, p.a.base, p.k, p.m, 1, a_pitch, 0, mmr::GT_BK, mmr::GT_MN, "lhs"))
       return cleanup(e);
-    if (h->mode == 1) {
-      if (cudaMalloc(&h->d_nf, 2 * sizeof(unsigned int)) != cudaSuccess ||
-          cudaMemset(h->d_nf, 0, 2 * sizeof(unsigned int)) != cudaSuccess)
-        return cleanup(fail(MMR_ERR_CUDA, "allocating the non-finite flag failed"));
-      g.nf = h->d_nf;
-      fill_simt_params(p, &h->sp);
-    }
+    g.a = reinterpret_cast<const float*>(p.a.base);
+    g.a_m = a_pitch;
+    g.b = reinterpret_cast<const float*>(p.b.base);
+    g.b_k = p.b.s_r;
     const void* fn = h->mode ? reinterpret_cast<const void*>(mmr::mmr_gemv_tc_kernel<1>)
                              : reinterpret_cast<const void*>(mmr::mmr_gemv_tc_kernel<0>);
     cudaError_t ce = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, h->smem);
@@ -1300,8 +1297,6 @@ int32_t mmr_gemm_run_on(mmr_gemm_handle* h, void* stream) {
         break;
       case MMR_FAMILY_GEMV:
         e = h->gemv_tc ? launch_gemv_tc(h, s) : launch_gemv(h, s);
-        if (e == cudaSuccess && h->gemv_tc && h->mode == 1)
-          e = mmr::launch_kernel(mmr::mmr_gemv_tc_fixup_kernel, dim3(h->sms), dim3(256), 0, s, dim3(1, 1, 1), h->sp, h->d_nf);
         break;
       case MMR_FAMILY_SIMT:
         e = mmr::launch_kernel(mmr::mmr_simt_gemm_exact_kernel, h->grid, h->block, 0, s, dim3(1, 1, 1), h->sp);
