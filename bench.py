@@ -220,6 +220,10 @@ def dist_init(args):
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # NCCL here only carries the handshakes, the max-over-ranks timings and
+    # the input all-gather of the e2e leg: no NVLink multicast (NVLS) buffers,
+    # which would stay bound to every rank's memory for the whole run.
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     return rank, world, local
 
 
