@@ -113,6 +113,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
     mbar_init(recv, GV_KSPLIT);
     fence_mbar_init();
   }
+  // the tensor map is a kernel parameter: fetch it before waiting on the
+  // previous kernel
+  if (warp == GV_CONSUMER_WARPS && lane == 0) tma_prefetch_desc(&tmB);
   __syncthreads();
   cluster_arrive_release();  // the receive barrier is ready; waited on before the first push
   griddep_wait();
@@ -121,7 +124,6 @@ __global__ void __launch_bounds__(GV_THREADS, 2) mmr_gemv_cluster_kernel(const _
   if (warp == GV_CONSUMER_WARPS) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
-      tma_prefetch_desc(&tmB);
       int issued = 0;
       for (int s = 0; s < nstages; ++s) {
         const int slot = s % kStages;
