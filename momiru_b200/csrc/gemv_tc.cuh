@@ -56,8 +56,9 @@ constexpr int GT_KSPLIT = 4;                         // K-slices per strip (clus
 __host__ __device__ constexpr int gt_stages(int mode) { return mode ? 4 : 11; }
 // K per TMEM accumulation chunk; chunks are summed with RN adds. The tensor
 // core's own f32 accumulation is not round-to-nearest (about one unit in the
-// last place per instruction, of either sign); with the two interleaved
-// accumulators below, a 256-wide chunk adds 16 instructions per accumulator.
+// last place per instruction, of either sign); with the two issuers below,
+// each with its own accumulator, a 256-wide chunk adds 16 instructions per
+// accumulator.
 constexpr int GT_CHUNK = 256;
 constexpr int GT_B_BYTES = GT_BK * GT_COLS * 4;      // 16 KiB
 constexpr int GT_A_BYTES = GT_MN * GT_BK * 4;        // 2 KiB
@@ -66,29 +67,28 @@ constexpr int GT_LOAD_BYTES = GT_B_BYTES + GT_A_BYTES;  // what TMA brings per s
 __host__ __device__ constexpr int gt_stage_bytes(int mode) { return GT_LOAD_BYTES + (mode ? GT_A_BYTES : 0); }
 // StrictFp32 split warps: GT_SPLIT_GROUPS groups of 8, taking stages in
 // turn (one group keeps ahead of the MMA issuer).
-constexpr int GT_EPI_WARPS = 4, GT_PRODUCER_WARP = 4, GT_MMA_WARP = 5, GT_SPLIT_WARP0 = 6;
+constexpr int GT_EPI_WARPS = 4, GT_PRODUCER_WARP = 4, GT_MMA_WARP0 = 5, GT_ISSUERS = 2, GT_SPLIT_WARP0 = 7;
 constexpr int GT_SPLIT_GROUP_WARPS = 8, GT_SPLIT_GROUPS = 1;
 __host__ __device__ constexpr int gt_threads(int mode) {
   return 32 * (GT_SPLIT_WARP0 + (mode ? GT_SPLIT_GROUPS * GT_SPLIT_GROUP_WARPS : 0));
 }
 constexpr int GT_PART_BYTES = GT_MN * GT_COLS * 4;   // the CTA's partial sums [m][n]
-// TMEM: two chunk buffers, each holding GT_ILV accumulators of GT_MN columns
-// (TF32) or 2 * GT_MN (StrictFp32: [hi(A) | lo(A)] products); k-step kk of a
-// stage accumulates into set kk mod GT_ILV. An MMA that adds into the
-// accumulator of the one before it waits for that one to finish, and a
-// 128 x 16 (or x 32) instruction is short next to that latency, so
-// alternating sets keeps GT_ILV instructions in flight. Then, StrictFp32
-// only, lo(B) of each ring stage in GT_BK columns (lane = strip column,
-// column = k).
-constexpr int GT_ILV = 2, GT_ACC_BUFS = 2;
+// MMA issue: GT_ISSUERS warps, issuer j taking the stages s = j mod
+// GT_ISSUERS of each chunk into an accumulator of its own. An MMA that adds
+// into the accumulator of the one before it waits for that one to finish, and
+// a 128 x 16 (or x 32) instruction is short next to that latency; two chains
+// keep two in flight. TMEM: for each of two chunk buffers, one accumulator
+// per issuer of GT_MN columns (TF32) or 2 * GT_MN (StrictFp32: [hi(A) | lo(A)]
+// products); then, StrictFp32 only, lo(B) of each ring stage in GT_BK
+// columns (lane = strip column, column = k).
+constexpr int GT_ACC_BUFS = 2 * GT_ISSUERS;  // buffer (chunk parity, issuer)
 __host__ __device__ constexpr int gt_acc_cols(int mode) { return mode ? 2 * GT_MN : GT_MN; }
-__host__ __device__ constexpr int gt_buf_cols(int mode) { return GT_ILV * gt_acc_cols(mode); }
-constexpr int GT_LO_COL0 = GT_ACC_BUFS * GT_ILV * 2 * GT_MN;
+constexpr int GT_LO_COL0 = GT_ACC_BUFS * 2 * GT_MN;
 __host__ __device__ constexpr int gt_pow2_cols(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
 __host__ __device__ constexpr int gt_tmem_cols(int mode) {
-  return gt_pow2_cols(mode ? GT_LO_COL0 + gt_stages(1) * GT_BK : GT_ACC_BUFS * GT_ILV * GT_MN);
+  return gt_pow2_cols(mode ? GT_LO_COL0 + gt_stages(1) * GT_BK : GT_ACC_BUFS * GT_MN);
 }
-static_assert(GT_ACC_BUFS * gt_buf_cols(0) <= gt_tmem_cols(0), "TF32 accumulators exceed the TMEM allocation");
+static_assert(GT_ACC_BUFS * gt_acc_cols(0) <= gt_tmem_cols(0), "TF32 accumulators exceed the TMEM allocation");
 static_assert(GT_LO_COL0 + gt_stages(1) * GT_BK <= 512, "lo(B) ring exceeds TMEM");
 static_assert(GT_LOAD_BYTES % 1024 == 0 && GT_A_BYTES % 1024 == 0, "stages and panels keep 1024-byte alignment");
 
@@ -98,7 +98,7 @@ constexpr int GT_BAR_BYTES = 512;
 __host__ __device__ constexpr int gt_smem_bytes(int mode) {
   return gt_stages(mode) * gt_stage_bytes(mode) + GT_PART_BYTES + GT_BAR_BYTES + 1024;
 }
-static_assert((3 * 11 + 2 * GT_ACC_BUFS + 2) * 8 + 8 <= GT_BAR_BYTES, "barrier area");
+static_assert((3 * 11 + 2 * GT_ACC_BUFS + GT_ISSUERS + 1) * 8 + 8 <= GT_BAR_BYTES, "barrier area");
 static_assert(gt_smem_bytes(0) <= 227 * 1024 && gt_smem_bytes(1) <= 227 * 1024, "shared memory");
 
 struct GemvTcParams {
@@ -141,8 +141,8 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
   constexpr int kAcc = GT_ACC_BUFS;
   uint64_t* acc_full = bars + 3 * S;     // [kAcc] MMA -> epilogue
   uint64_t* acc_empty = acc_full + kAcc; // [kAcc] epilogue -> MMA
-  uint64_t* drain = acc_full + 2 * kAcc;
-  uint64_t* recv = drain + 1;        // GT_KSPLIT arrivals: every K-slice's partial is in `part`
+  uint64_t* drain = acc_full + 2 * kAcc;  // [GT_ISSUERS]
+  uint64_t* recv = drain + GT_ISSUERS;    // GT_KSPLIT arrivals: every K-slice's partial is in `part`
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(recv + 1);
   uint32_t* nonfinite_seen = tmem_slot + 1;  // StrictFp32: an input of this strip held inf/NaN
 
@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
       mbar_init(&acc_full[a], 1);
       mbar_init(&acc_empty[a], GT_EPI_WARPS);
     }
-    mbar_init(drain, 1);
+    for (int j = 0; j < GT_ISSUERS; ++j) mbar_init(&drain[j], 1);
     mbar_init(recv, GT_KSPLIT);
     *nonfinite_seen = 0u;
     fence_mbar_init();
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmA);
   }
-  if (warp == GT_MMA_WARP) {
+  if (warp == GT_MMA_WARP0) {
     tmem_alloc(tmem_slot, gt_tmem_cols(MODE));
     tmem_relinquish();
   }
@@ -194,30 +194,41 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
     // ------------------------------------------------------------ epilogue
     // Thread (warp, lane) owns column n = warp * 32 + lane of the strip (TMEM
     // lane) and its GT_MN sums; each K-chunk is added with RN adds.
-    int acc = 0;
-    uint32_t acc_phase = 0;
+    // Chunk c: issuer j's accumulator in buffer (c mod 2, j), added in
+    // issuer order; an issuer with no stage in the last chunk is skipped by
+    // both sides.
     for (int c = 0; c < nchunks; ++c) {
-      if (!mbar_wait(&acc_full[acc], acc_phase, ctl, kDevTimeoutAcc)) break;
-      tc_fence_after();
-      // The buffer's GT_ILV * (1 or 2) column groups of GT_MN, added in a
-      // fixed order.
-      constexpr int kGroups = gt_buf_cols(MODE) / GT_MN;
-      const uint32_t t = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc * gt_buf_cols(MODE));
-      uint32_t r[kGroups][16];
+      const int c_end = min(nstages, (c + 1) * kStagesPerChunk);
+      const uint32_t acc_phase = static_cast<uint32_t>(c >> 1) & 1u;
+      float v[GT_MN];
+      bool ok = true;
 #pragma unroll
-      for (int g = 0; g < kGroups; ++g) tmem_ld_32x32b_x16(t + g * GT_MN, r[g]);
-      tmem_ld_wait();
+      for (int j = 0; j < GT_ISSUERS; ++j) {
+        if (c * kStagesPerChunk + j >= c_end) break;
+        const int acc = (c & 1) * GT_ISSUERS + j;
+        if (!mbar_wait(&acc_full[acc], acc_phase, ctl, kDevTimeoutAcc)) { ok = false; break; }
+        tc_fence_after();
+        // StrictFp32: columns m and GT_MN + m hold the [hi(A) | lo(A)] products
+        constexpr int kGroups = gt_acc_cols(MODE) / GT_MN;
+        const uint32_t t = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(acc * gt_acc_cols(MODE));
+        uint32_t r[kGroups][16];
 #pragma unroll
-      for (int i = 0; i < GT_MN; ++i) {
-        float v = __uint_as_float(r[0][i]);
+        for (int g = 0; g < kGroups; ++g) tmem_ld_32x32b_x16(t + g * GT_MN, r[g]);
+        tmem_ld_wait();
 #pragma unroll
-        for (int g = 1; g < kGroups; ++g) v = __fadd_rn(v, __uint_as_float(r[g][i]));
-        sum[i] = __fadd_rn(sum[i], v);
+        for (int i = 0; i < GT_MN; ++i) {
+          float x = __uint_as_float(r[0][i]);
+#pragma unroll
+          for (int g = 1; g < kGroups; ++g) x = __fadd_rn(x, __uint_as_float(r[g][i]));
+          v[i] = j == 0 ? x : __fadd_rn(v[i], x);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[acc]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
-      if (++acc == kAcc) { acc = 0; acc_phase ^= 1u; }
+      if (!ok) break;
+#pragma unroll
+      for (int i = 0; i < GT_MN; ++i) sum[i] = __fadd_rn(sum[i], v[i]);
     }
   } else if (warp == GT_PRODUCER_WARP) {
     // ---------------------------------------------------------- producer
@@ -245,8 +256,9 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
         }
       }
     }
-  } else if (warp == GT_MMA_WARP) {
-    // -------------------------------------------------------- MMA issuer
+  } else if (warp < GT_MMA_WARP0 + GT_ISSUERS) {
+    // ------------------------------------------------------- MMA issuers
+    const int jw = warp - GT_MMA_WARP0;  // this issuer takes stages s = jw mod GT_ISSUERS
     if (lane == 0) {
       // B tile (MN-major) x the A panel, or x [A panel | lo(A)] in StrictFp32
       constexpr uint32_t idesc = idesc_tf32(GT_COLS, gt_acc_cols(MODE), true, false);
@@ -256,16 +268,19 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
       const uint64_t b_desc0 = smem_desc(smem_u32(ops) + GT_B_BYTES, 16u, 1024u, 2u);    // A panel, K-major
       constexpr uint64_t kStageStep = kStage >> 4;
       uint64_t* const ready = MODE ? split_done : full;
-      int stage = 0, acc = 0;
-      uint32_t phase = 0, acc_phase = 0;
       bool ok = true, issued_any = false;
       for (int c = 0; ok && c < nchunks; ++c) {
+        const int s_end = min(nstages, (c + 1) * kStagesPerChunk);
+        if (c * kStagesPerChunk + jw >= s_end) break;  // no stage of this chunk (only the last can lack one)
+        const int acc = (c & 1) * GT_ISSUERS + jw;
+        const uint32_t acc_phase = static_cast<uint32_t>(c >> 1) & 1u;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, ctl, kDevTimeoutAcc)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * gt_buf_cols(MODE));
-        uint32_t accumulate = 0u;  // bit j: set j of this buffer holds a partial sum
-        const int s_end = min(nstages, (c + 1) * kStagesPerChunk);
-        for (int s = c * kStagesPerChunk; s < s_end; ++s) {
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * gt_acc_cols(MODE));
+        uint32_t accumulate = 0u;
+        for (int s = c * kStagesPerChunk + jw; s < s_end; s += GT_ISSUERS) {
+          const int stage = s % S;
+          const uint32_t phase = static_cast<uint32_t>(s / S) & 1u;
           if (!mbar_wait(&ready[stage], phase, ctl, MODE ? kDevTimeoutXform : kDevTimeoutFull)) { ok = false; break; }
           tc_fence_after();
           const uint64_t so = static_cast<uint64_t>(stage) * kStageStep;
@@ -273,27 +288,23 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
           for (int kk = 0; kk < GT_BK / 8; ++kk) {
             const uint64_t ad = a_desc0 + so + kk * (1024u >> 4);
             const uint64_t bd = b_desc0 + so + kk * (32u >> 4);
-            const int set = kk % GT_ILV;
-            const uint32_t d_set = d_tmem + static_cast<uint32_t>(set * gt_acc_cols(MODE));
-            umma_tf32(d_set, ad, bd, idesc, (accumulate >> set) & 1u);  // hi(B) x hi(A) [| lo(A)]
-            if (MODE) {                                                // lo(B) x hi(A)
+            umma_tf32(d_tmem, ad, bd, idesc, accumulate);  // hi(B) x hi(A) [| lo(A)]
+            if (MODE) {                                    // lo(B) x hi(A)
               const uint32_t lo_b = tmem_base + static_cast<uint32_t>(GT_LO_COL0 + stage * GT_BK + kk * 8);
-              umma_tf32_ts(d_set, lo_b, bd, idesc_ts, 1u);
+              umma_tf32_ts(d_tmem, lo_b, bd, idesc_ts, 1u);
             }
-            accumulate |= 1u << set;
+            accumulate = 1u;
           }
           issued_any = true;
           umma_commit(&empty[stage]);
-          if (++stage == S) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
         umma_commit(&acc_full[acc]);
-        if (++acc == kAcc) { acc = 0; acc_phase ^= 1u; }
       }
       if (issued_any) {
-        // Every MMA must have finished before TMEM is freed.
-        umma_commit(drain);
-        const uint32_t a = smem_u32(drain);
+        // Every MMA of this issuer must have finished before TMEM is freed.
+        umma_commit(&drain[jw]);
+        const uint32_t a = smem_u32(&drain[jw]);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(a, 0u)) {
           if (globaltimer_ns() - t0 > p.timeout_ns) { atomicCAS(p.err, 0, kDevTimeoutDrain); break; }
@@ -362,7 +373,7 @@ __global__ void __launch_bounds__(gt_threads(MODE), 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == GT_MMA_WARP) {
+  if (warp == GT_MMA_WARP0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, gt_tmem_cols(MODE));
   }
