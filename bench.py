@@ -359,7 +359,8 @@ def run_workload(args, rank, world, local):
         lines.append({
             "metric": name, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak" if args.workload == "c5a" and world > 1 else "replicas" if world > 1 else "n/a",
+            "scaling": ("weak" if args.workload == "c5a" else "strong" if args.workload == "c4" else "replicas")
+                       if world > 1 else "n/a",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (SplitMix64)", "config": cfg,
             "math": "3xTF32 (StrictFp32)" if args.mode == "strict" else "TF32",
             "family": handles[0].family,
@@ -387,12 +388,36 @@ def run_workload(args, rank, world, local):
         x, wt = dv(rng.randn((4096, 4096), 1, 0.02)), dv(rng.randn((4096, 12288), 2, 0.02))
         out = DeviceView.empty((4096, 11008), dev)
         xt, wtt, ot = x.torch_view(), wt.torch_view(), out.torch_view()
+        lhs, rhs = x.transpose(), wt.narrow(1, 0, 11008)
+        cfg = {"workload": "c4_xT_4096_wslice_11008", "l2": "inputs 245 MB > L2"}
+        if world > 1:
+            # Column blocks of 256-column units, each rank keeping its block of
+            # the output (no replication, so no collective): strong scaling.
+            from momiru_b200.sharding import column_block_views
+            rhs, out_l, _, c0, c1 = column_block_views(node, lhs, rhs, out, None, rank, world)
+            cfg["parallelism"] = f"column-block x{world}, output kept sharded, no collective"
+            cfg["columns"] = [c0, c1]
+            g = BoundGemm(node, lhs, rhs, out_l, stream=stream.cuda_stream)
+        else:
+            g = BoundGemm(node, lhs, rhs, out, stream=stream.cuda_stream)
         lib = {"cublas_tf32": (True, lambda: torch.matmul(xt.t(), wtt[:, :11008], out=ot)),
                "cublas_fp32": (False, lambda: torch.matmul(xt.t(), wtt[:, :11008], out=ot))}
-        timed([BoundGemm(node, x.transpose(), wt.narrow(1, 0, 11008), out, stream=stream.cuda_stream)],
-              2.0 * 4096 * 4096 * 11008, 4 * (4096 * 4096 + 2 * 4096 * 11008),
-              "C4 strided views 4096x4096x11008 TFLOP/s",
-              {"workload": "c4_xT_4096_wslice_11008", "l2": "inputs 245 MB > L2"}, "tensor", lib)
+        timed([g], 2.0 * 4096 * 4096 * 11008, 4 * (4096 * 4096 + 2 * 4096 * 11008),
+              "C4 strided views 4096x4096x11008 TFLOP/s", cfg, "tensor", lib)
+        if world > 1:
+            # every block against the oracle on sampled rows: gather the blocks
+            # on rank 0 (after the timed region)
+            blk = out.torch_view()[:, c0:c1].contiguous()
+            sizes = [torch.tensor([blk.shape[1]], device=f"cuda:{dev}") for _ in range(world)]
+            dist.all_gather(sizes, torch.tensor([blk.shape[1]], device=f"cuda:{dev}"))
+            widest = max(int(t.item()) for t in sizes)
+            pad = torch.zeros((4096, widest), dtype=torch.float32, device=f"cuda:{dev}")
+            pad[:, :blk.shape[1]] = blk
+            blocks = [torch.empty_like(pad) for _ in range(world)]
+            dist.all_gather(blocks, pad)
+            if rank == 0:
+                full = torch.cat([b[:, :int(t.item())] for b, t in zip(blocks, sizes)], dim=1).cpu().numpy()
+                lines[-1]["parity"] = c4_sampled_parity(full, x.to_host(), wt.to_host()[:, :11008], args.mode)
     elif w == "c5a":
         b0, b1 = batch_shards(512, world)[rank]
         nb = b1 - b0
@@ -455,6 +480,21 @@ def sampled_parity(out_t, a_h, b_h, bias_h, mode, nrows=32):
     tol = 1e-5 if mode == "strict" else 2e-3
     return {"rows": int(len(rows)), "rel_frob": err, "tol": tol, "ok": err <= tol,
             "against": "oracle (restated reference gemm + bias + ReLU)"}
+
+
+def c4_sampled_parity(full, x_h, w_h, mode, nrows=32):
+    """The column-sharded C4 output, gathered from every rank (`full`, host
+    [4096, 11008]): `nrows` rows against the oracle on A = X^T, B = W[:, :11008]."""
+    from oracle import oracle as O
+    O.build()
+    rows = np.unique(np.linspace(0, full.shape[0] - 1, nrows).astype(np.int64))
+    ref = O.matmul(x_h.T, w_h, rows=rows, nthreads=os.cpu_count() or 1).astype(np.float64)
+    got = full[rows].astype(np.float64)
+    den = float(np.linalg.norm(ref))
+    err = float(np.linalg.norm(got - ref) / (den if den > 0 else 1.0))
+    tol = 1e-5 if mode == "strict" else 2e-3
+    return {"rows": int(len(rows)), "rel_frob": err, "tol": tol, "ok": err <= tol,
+            "against": "oracle (restated reference gemm), blocks of every rank"}
 
 
 def hg_panels(m, panels):

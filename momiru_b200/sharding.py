@@ -63,6 +63,30 @@ def local_shard(desc, rank: int, world: int):
     return local, c0.value, c1.value, off.value
 
 
+def column_block_views(node, lhs, rhs, out, bias=None, rank: int = 0, world: int = 1):
+    """Rank `rank`'s share of a column-sharded node whose output stays
+    sharded: each rank computes and keeps out[..., c0:c1], so no collective
+    runs (the C4 projection shape across GPUs). Returns (rhs_block,
+    out_block, bias_block, c0, c1): zero-copy views narrowed to the rank's
+    column block, exactly the ones the library's host-only narrowing
+    (mmr_shard_local_desc) produces, which is checked here."""
+    from . import _abi, execution
+    local, c0, c1, _ = local_shard(execution._desc(node, lhs, rhs, out, bias, None), rank, world)
+    n = c1 - c0
+    rb = rhs.narrow(-2 if node.transpose_rhs else -1, c0, n)
+    ob = out.narrow(-1, c0, n)
+    bb = bias.narrow(-1, c0, n) if bias is not None else None
+    for mine, theirs in ((rb, local.rhs), (ob, local.out)):
+        v = mine.to_abi()
+        same = (v.address + v.base_offset_bytes == theirs.address + theirs.base_offset_bytes
+                and list(v.dims[:v.rank]) == list(theirs.dims[:theirs.rank])
+                and list(v.strides[:v.rank]) == list(theirs.strides[:theirs.rank]))
+        if not same:
+            raise execution.InvalidArgument("column block disagrees with mmr_shard_local_desc",
+                                            _abi.ERR_INVALID_ARGUMENT)
+    return rb, ob, bb, c0, c1
+
+
 def exchange_replica_handles(mine, group=None) -> list:
     """Bind-time exchange: every rank contributes the IPC handles of its output
     replica and its completion-signal array, as ((handle bytes, offset),

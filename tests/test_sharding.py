@@ -170,3 +170,32 @@ def test_local_shard_rejects_bad_ranks():
     d.out = _host_view(np.zeros(8, np.float32))
     with pytest.raises(InvalidShape):
         local_shard(d, 0, 2)  # a vector rhs has no columns to shard
+
+
+def test_column_block_views_match_the_library_narrowing():
+    """The C4 projection shape (A = X^T view, B = a column slice of a wider
+    buffer) split over 8 ranks with the output kept sharded: every rank's
+    views are the library's narrowing (mmr_shard_local_desc), and the blocks
+    tile the 11008 output columns in 256-column units. Host only."""
+    from momiru_b200 import DeviceBuffer, DeviceView, MatMulNode
+    from momiru_b200.sharding import column_block_views, column_shards
+    g = 1 << 32
+    x = DeviceView.contiguous(DeviceBuffer(1 * g, 4 * 4096 * 4096, 0), (4096, 4096))
+    w = DeviceView.contiguous(DeviceBuffer(2 * g, 4 * 4096 * 12288, 0), (4096, 12288))
+    out = DeviceView.contiguous(DeviceBuffer(3 * g, 4 * 4096 * 11008, 0), (4096, 11008))
+    blocks = []
+    for rank in range(8):
+        rb, ob, bb, c0, c1 = column_block_views(MatMulNode(), x.transpose(), w.narrow(1, 0, 11008), out,
+                                                None, rank, 8)
+        assert bb is None and (c0, c1) == column_shards(11008, 8)[rank]
+        assert rb.dims == (4096, c1 - c0) and rb.strides == (12288, 1) and rb.offset == c0
+        assert ob.dims == (4096, c1 - c0) and ob.strides == (11008, 1) and ob.offset == c0
+        blocks.append((c0, c1))
+    assert blocks[0][0] == 0 and blocks[-1][1] == 11008
+    assert all(a[1] == b[0] for a, b in zip(blocks, blocks[1:]))
+    # transpose_rhs: the rhs buffer is [n, k] and its rows are the columns being dealt
+    wt = DeviceView.contiguous(DeviceBuffer(4 * g, 4 * 1024 * 512, 0), (1024, 512))
+    o2 = DeviceView.contiguous(DeviceBuffer(5 * g, 4 * 300 * 1024, 0), (300, 1024))
+    a2 = DeviceView.contiguous(DeviceBuffer(6 * g, 4 * 300 * 512, 0), (300, 512))
+    rb, ob, _, c0, c1 = column_block_views(MatMulNode(transpose_rhs=True), a2, wt, o2, None, 1, 2)
+    assert (c0, c1) == (512, 1024) and rb.dims == (512, 512) and rb.offset == 512 * 512
