@@ -623,35 +623,100 @@ def main():
             hg.replay()
     else:
         from cuda.bindings import runtime as cudart
+        from momiru_b200.sharding import ReplicatedColumnGemm
         r0, r1 = rank * n // world, (rank + 1) * n // world
-        a_slab = torch.empty((r1 - r0, n), dtype=torch.float32, device=dev)
-        c_block = torch.empty((n, ncols), dtype=torch.float32).pin_memory()
+        even = n % world == 0  # equal slabs for the all-gather; otherwise every rank copies all of A
         e2e_path = ("each rank: its A row slab in, A all-gathered over NVLink, its B/bias column block in, "
-                    "replicated GEMM, its C column block out")
+                    "replicated GEMM, its C column block out; two buffer lanes, so step i+1's copies in and "
+                    "all-gather run beside step i's GEMM and copy out")
 
-        def copy2d(dst, dpitch, src, spitch, width, rows, kind):
+        def copy2d(dst, dpitch, src, spitch, width, rows, kind, st):
             if width and rows:
-                err, = cudart.cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, kind, stream.cuda_stream)
+                err, = cudart.cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, rows, kind, st.cuda_stream)
                 if err != cudart.cudaError_t.cudaSuccess:
                     raise RuntimeError(f"cudaMemcpy2DAsync: {err}")
 
-        even = n % world == 0  # equal slabs for the all-gather; otherwise every rank copies all of A
+        def make_lane(a_, b_, bias_, out_, g_):
+            ev = lambda: torch.cuda.Event()  # noqa: E731
+            return {"a": a_, "b": b_, "bias": bias_, "out": out_, "g": g_,
+                    "slab": torch.empty((r1 - r0, n), dtype=torch.float32, device=dev),
+                    "c": torch.empty((n, ncols), dtype=torch.float32).pin_memory(),
+                    "slab_ev": ev(), "in": ev(), "ag": ev(), "gemm": ev(), "out_ev": ev(), "used": False}
+
+        # Lane 1: a second set of device buffers and a second replicated handle
+        # (its own replicas, signal array and IPC exchange).
+        a2, b2, bias2, out2 = (torch.empty_like(t) for t in (a_t, b_t, bias_t, out_t))
+        g2 = ReplicatedColumnGemm(node, DeviceView.contiguous(DeviceBuffer.from_torch(a2), (n, n)),
+                                  DeviceView.contiguous(DeviceBuffer.from_torch(b2), (n, n)),
+                                  DeviceView.contiguous(DeviceBuffer.from_torch(out2), (n, n)),
+                                  DeviceView.contiguous(DeviceBuffer.from_torch(bias2), (n,)),
+                                  stream=stream.cuda_stream)
+        lanes = [make_lane(a_t, b_t, bias_t, out_t, g), make_lane(a2, b2, bias2, out2, g2)]
+        s_in, s_ag, s_out = (torch.cuda.Stream(dev) for _ in range(3))
+        fence = torch.zeros(1, dtype=torch.float32, device=dev)
+        step_no = [0]
+
+        def e2e_begin():
+            # the side streams start after whatever the caller's stream holds
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            for st in (s_in, s_ag, s_out):
+                st.wait_event(ev)
+
+        def e2e_end():
+            for ln in lanes:
+                if ln["used"]:
+                    stream.wait_event(ln["out_ev"])
 
         def e2e_step():
+            ln = lanes[step_no[0] % 2]
+            step_no[0] += 1
+            # copies in, once this lane's previous GEMM has read its inputs
+            if ln["used"]:
+                s_in.wait_event(ln["gemm"])
+            with torch.cuda.stream(s_in):
+                if even:
+                    ln["slab"].copy_(a_pin[r0:r1], non_blocking=True)
+                    ln["slab_ev"].record(s_in)
+                else:
+                    ln["a"].copy_(a_pin, non_blocking=True)
+                copy2d(ln["b"].data_ptr() + 4 * c0, 4 * n, b_pin.data_ptr() + 4 * c0, 4 * n, 4 * ncols, n,
+                       cudart.cudaMemcpyKind.cudaMemcpyHostToDevice, s_in)
+                if ncols:
+                    ln["bias"][c0:c1].copy_(bias_pin[c0:c1], non_blocking=True)
+                ln["in"].record(s_in)
             if even:
-                a_slab.copy_(a_pin[r0:r1], non_blocking=True)
-                dist.all_gather_into_tensor(a_t, a_slab)
-            else:
-                a_t.copy_(a_pin, non_blocking=True)
-            copy2d(b_t.data_ptr() + 4 * c0, 4 * n, b_pin.data_ptr() + 4 * c0, 4 * n, 4 * ncols, n,
-                   cudart.cudaMemcpyKind.cudaMemcpyHostToDevice)
-            if ncols:
-                bias_t[c0:c1].copy_(bias_pin[c0:c1], non_blocking=True)
-            g.replay()
-            copy2d(c_block.data_ptr(), 4 * ncols, out_t.data_ptr() + 4 * c0, 4 * n, 4 * ncols, n,
-                   cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+                with torch.cuda.stream(s_ag):
+                    s_ag.wait_event(ln["slab_ev"])
+                    dist.all_gather_into_tensor(ln["a"], ln["slab"], async_op=True).wait()
+                    ln["ag"].record(s_ag)
+            # The GEMM stores into every rank's replica of this lane, so every
+            # rank must have finished copying out this lane's previous result:
+            # a one-float all-reduce after this rank's own copy out orders it.
+            stream.wait_event(ln["in"])
+            if even:
+                stream.wait_event(ln["ag"])
+            if ln["used"]:
+                stream.wait_event(ln["out_ev"])
+                dist.all_reduce(fence)
+            ln["g"].replay()
+            ln["gemm"].record(stream)
+            s_out.wait_event(ln["gemm"])
+            copy2d(ln["c"].data_ptr(), 4 * ncols, ln["out"].data_ptr() + 4 * c0, 4 * n, 4 * ncols, n,
+                   cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost, s_out)
+            ln["out_ev"].record(s_out)
+            ln["used"] = True
 
-    e2e_step()
+    if world == 1:
+        def e2e_begin():
+            pass
+
+        def e2e_end():
+            pass
+    e2e_begin()
+    for _ in range(1 if world == 1 else 2):  # warm-up (each lane once across ranks)
+        e2e_step()
+    e2e_end()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -659,8 +724,10 @@ def main():
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    e2e_begin()
     for _ in range(args.e2e_steps):
         e2e_step()
+    e2e_end()
     e1.record(stream)
     torch.cuda.synchronize()
     clocks.active = False
@@ -673,6 +740,8 @@ def main():
     if world == 1:
         hg.quiesce_or_abort(60)
         hg.close()
+    else:
+        g2.quiesce_or_abort(60)
     clocks.stop()
 
     # ------------------------------------------------------ correctness
@@ -688,7 +757,11 @@ def main():
     # the host copy of the result is this rank's column block of the replica
     e2e_host_ok = None
     if world > 1:
-        bad = torch.tensor([0 if torch.equal(c_block, out_t[:, c0:c1].cpu()) else 1], device=dev)
+        # each lane's host block equals its replica's block, and both lanes
+        # computed the same product
+        ok = torch.equal(out2, out_t) and all(
+            torch.equal(ln["c"], ln["out"][:, c0:c1].cpu()) for ln in lanes if ln["used"])
+        bad = torch.tensor([0 if ok else 1], device=dev)
         dist.all_reduce(bad, op=dist.ReduceOp.SUM)
         e2e_host_ok = int(bad.item()) == 0
     parity = None
@@ -741,6 +814,7 @@ def main():
         line["cpu_baseline"] = cpu_baseline_sample(a_h, b_h, bias_h, args.cpu_seconds)
     g.close()
     if world > 1:
+        g2.close()
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
