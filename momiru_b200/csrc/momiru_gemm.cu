@@ -729,13 +729,10 @@ int32_t derive_launch(const Plan& p, const TmaLayout& t, int32_t fam, int sms, L
       // 16384 82 / 61 / 83 / 100 us; TF32 1024^2 x 8192 60 / 45 us at
       // 4096 / 1024 K. Each part parks a 256 KB partial tile in L2 and the
       // last one reads them all back, which is what shorter parts lose on.
-      // A short K (3xTF32) may still be cut into up to four parts of at least
-      // 128 K: with so few parts the last one reads back at most three
-      // partial tiles, and 512^3 otherwise runs on four pairs.
       const int64_t min_part_k = L.mode ? 512 : 1024;
-      const int64_t parts = L.mode ? std::max<int64_t>(p.k / min_part_k, std::min<int64_t>(4, p.k / 128))
-                                   : p.k / min_part_k;
-      L.split = L.tiles < sms / 2 ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / L.tiles, parts)) : 1;
+      L.split = L.tiles < sms / 2
+                    ? std::max<int64_t>(1, std::min<int64_t>((sms / 2) / L.tiles, p.k / min_part_k))
+                    : 1;
       L.npairs = std::min<int64_t>(L.tiles, sms / 2) * L.split;
       L.grid = dim3(unsigned(2 * L.npairs));
       // Whole rounds of tiles stay round-robin. When the tiles do not fill

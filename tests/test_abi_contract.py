@@ -344,13 +344,10 @@ def test_plan_launch_records_the_bound_launch_for_each_family():
     # small output with a long K: tiles split along K over several pairs
     s = plan_launch(MatMulNode(), fake((1024, 8192), 1), fake((8192, 1024), 2), fake((1024, 1024), 3))
     assert s.split_k > 1 and s.grid[0] == 2 * 16 * s.split_k
-    # 512^3 (four pair tiles, K = 512): StrictFp32 cuts K into four parts of 128 on 16 pairs;
-    # TF32 keeps its 1024-K minimum and does not split
-    s = plan_launch(MatMulNode(), fake((512, 512), 1), fake((512, 512), 2), fake((512, 512), 3))
-    assert s.split_k == 4 and s.grid[0] == 2 * 4 * 4 and s.partition == _abi.PARTITION_STREAM_K
-    check_launch_record(s)
-    s = plan_launch(tf32, fake((512, 512), 1), fake((512, 512), 2), fake((512, 512), 3))
-    assert s.split_k == 1 and s.grid[0] == 2 * 4
+    # 512^3 (four pair tiles, K = 512): K is not split below 512 (3xTF32) or 1024 (TF32)
+    for node in (MatMulNode(), tf32):
+        s = plan_launch(node, fake((512, 512), 1), fake((512, 512), 2), fake((512, 512), 3))
+        assert s.split_k == 1 and s.grid[0] == 2 * 4
 
 
 def test_check_launch_record_enforces_the_gpu_validator_rules():
